@@ -1,0 +1,533 @@
+#!/usr/bin/env python
+"""Benchmark of the hot path: embedded tokens/s of the ModernBERT-base varlen encoder on 1..8 B200s.
+
+``python bench.py --gpus N --steps K --warmup W`` (torchrun for N > 1, one rank per GPU).
+
+Workload (default): ModernBERT-base in bf16 (22 layers, hidden 768, 12 heads
+x 64, GeGLU 1152, global attention every 3rd layer with RoPE theta 160000, 128-token sliding
+window with theta 10000 elsewhere), random-init N(0, 0.02) weights; 4096 chunks per GPU with
+lengths uniform in [64, 512] and token ids uniform over the 50368-token vocabulary, packed varlen
+with cu_seqlens.  One step = the encoder forward over all 4096 chunks of the rank (mean-pooled,
+L2-normalised 768-d outputs).  Chunks shard by data parallelism with no collective (weak scaling:
+every rank embeds its own 4096 chunks).
+
+* ``value``: tokens/s with the ids already in HBM (``rv_embed_varlen_device``), CUDA events on
+  the launching stream around each step, L2 flushed between steps, max over ranks.
+* ``e2e``: the same through ``rv_embed_varlen`` with pinned host buffers (ids H2D and the
+  embeddings D2H inside the timed region), host clock around the synchronous call, max over ranks.
+* ``roofline``: the tcgen05 projection GEMMs, timed live by the library's own CUDA events on its
+  stream over the timed region; algorithmic FLOPs 2*M*N*K per launch.
+* ``cpu_baseline``: the numpy port of the reference fp32 CPU path (``oracle/``) on a bounded
+  sample of the same chunks, rank 0, N = 1.
+
+``--impl reference`` times that CPU port as the reference arm (rank 0 only).  Other workloads:
+``--workload long`` (config 3, fp16, 512 chunks of 2048..8192 tokens), ``--workload sweep``
+(config 4, 1M log-normal chunks sharded by token count), ``--workload scan`` (config 5, exact
+top-100 over a 10M x 768 bf16 database, 1024 queries, per-shard results merged after one NCCL
+all-gather).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "embedded tokens/sec (ModernBERT-base varlen)"
+UNIT = "tokens/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["encoder", "long", "sweep", "scan"], default="encoder")
+    ap.add_argument("--chunks", type=int, default=None, help="override chunks per GPU")
+    ap.add_argument("--max-batch-tokens", type=int, default=1 << 19)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ environment / ranks
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"], "bf16_sus": d["bf16_tflops_sustained"],
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sus": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def physical_gpu(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return int(vis.split(",")[local])
+        except (ValueError, IndexError):
+            return local
+    return local
+
+
+# ------------------------------------------------------------------ workloads
+def encoder_workload(args, rank):
+    from ripvec_b200 import MODERNBERT_BASE, synth
+
+    if args.workload == "long":
+        n = args.chunks or 512
+        lengths = synth.uniform_lengths(n, 2048, 8192, seed=2000 + rank)
+        name, dtype = "modernbert_base_long_fp16", "f16"
+        desc = f"{n} chunks, lengths U[2048,8192]"
+    else:
+        n = args.chunks or 4096
+        lengths = synth.uniform_lengths(n, 64, 512, seed=1000 + rank)
+        name, dtype = "modernbert_base_varlen", "bf16"
+        desc = f"{n} chunks, lengths U[64,512]"
+    ids, cu = synth.packed_ids(lengths, MODERNBERT_BASE.vocab, seed=3000 + rank)
+    return MODERNBERT_BASE, name, dtype, desc, lengths, ids, cu
+
+
+def sweep_shard(rank, world, n_chunks):
+    """1M log-normal chunks (median 180, sigma 0.8, clip [16,1024]) sharded by token count: sorted
+    by length descending, each chunk to the GPU with the fewest tokens so far."""
+    import heapq
+
+    from ripvec_b200 import synth
+
+    lengths = synth.lognormal_lengths(n_chunks, 180.0, 0.8, 16, 1024, seed=4242)
+    order = np.argsort(-lengths, kind="stable")
+    heap = [(0, g) for g in range(world)]
+    mine = []
+    for i in order:
+        load, g = heapq.heappop(heap)
+        if g == rank:
+            mine.append(i)
+        heapq.heappush(heap, (load + int(lengths[i]), g))
+    mine = np.asarray(sorted(mine), np.int64)
+    return lengths, mine
+
+
+# ------------------------------------------------------------------ reference arm (CPU port)
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(max(n)) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_encoder_rate(spec, w, lengths, ids, cu, budget_s: float, dtype=np.float32):
+    """Tokens/s of the numpy port of the reference fp32 CPU path over a bounded sample (whole
+    chunks in workload order until ``budget_s`` of CPU work, at least one chunk)."""
+    from oracle import modern_bert
+
+    cfg = modern_bert.ModernBertConfig(
+        hidden=spec.hidden, num_layers=spec.num_layers, num_heads=spec.num_heads, intermediate=spec.intermediate,
+        vocab=spec.vocab, max_position=spec.max_position, global_every_n=spec.global_every_n,
+        local_window=spec.local_window, global_rope_theta=spec.global_rope_theta,
+        local_rope_theta=spec.local_rope_theta, norm_eps=spec.norm_eps)
+    t0 = time.perf_counter()
+    tok = 0
+    n = 0
+    while n < len(lengths):
+        modern_bert.embed_sequence(w, cfg, ids[cu[n]:cu[n + 1]], dtype)
+        tok += int(lengths[n])
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return tok / dt, n, tok, dt
+
+
+def run_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    if args.workload == "scan":
+        return run_reference_scan(args)
+    from ripvec_b200 import synth
+
+    spec, name, dtype, desc, lengths, ids, cu = encoder_workload(args, 0)
+    w = synth.random_weights(spec, seed=1)
+    cores = blas_threads()
+    step_budget = 4.0
+    rates, samples = [], []
+    for s in range(args.warmup + args.steps):
+        # each step: a bounded sample of the workload's chunks, rotating through the workload
+        off = (s * 7) % max(1, len(lengths) - 16)
+        r, n, tok, dt = cpu_encoder_rate(spec, w, lengths[off:], ids[cu[off]:], cu[off:] - cu[off], step_budget)
+        if s >= args.warmup:
+            rates.append((tok, dt))
+            samples.append(n)
+    tok = sum(t for t, _ in rates)
+    dt = sum(d for _, d in rates)
+    value = tok / dt
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random token ids, random-init N(0,0.02) weights)",
+            "config": {"workload": name, "model": "ModernBERT-base", "chunks_per_gpu": len(lengths),
+                       "lengths": desc, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{sum(samples)} whole chunks ({tok} tokens) of the workload over {args.steps} steps"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_scan(args):
+    from oracle import scan as oscan
+    from ripvec_b200 import synth
+
+    n_rows, dim, nq = 10_000_000, 768, 1024
+    cores = blas_threads()
+    # bounded sample: the reference algorithm (f32 GEMV + full sort) over a slice of the database
+    sample = 200_000
+    db = synth.normalized_gaussian(sample, dim, seed=77)
+    q = synth.normalized_gaussian(8, dim, seed=78)
+    times = []
+    for s in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        for qi in range(q.shape[0]):
+            oscan.rank(db, q[qi], -1.0)
+        dt = time.perf_counter() - t0
+        if s >= args.warmup:
+            times.append(dt)
+    per_q_row = sum(times) / (args.steps * q.shape[0] * sample)
+    qps = 1.0 / (per_q_row * n_rows)
+    line = {"metric": "exact cosine top-100 queries/sec (10M x 768 bf16)", "value": qps, "unit": "queries/s",
+            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * sum(times) / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic normalised Gaussian rows",
+            "config": {"workload": "scan_topk", "rows": n_rows, "dim": dim, "queries": nq},
+            "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": cores, "kind": "port",
+                             "sample": f"{q.shape[0]} queries x {sample} rows per step, scaled to {n_rows} rows"},
+            "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+def traffic_per_flop():
+    """DRAM bytes per algorithmic GEMM FLOP from the committed ncu summary, or None."""
+    p = ROOT / "profiles" / "gemm_tc_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d["dram_bytes"] / d["flops"]
+
+
+def run_encoder(args):
+    import torch
+
+    from ripvec_b200 import EmbedBackend, synth
+    from ripvec_b200 import _lib as L
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    if args.workload == "sweep":
+        from ripvec_b200 import MODERNBERT_BASE
+
+        n_total = args.chunks or 1_000_000
+        all_len, mine = sweep_shard(rank, world, n_total)
+        lengths = all_len[mine]
+        ids, cu = synth.packed_ids(lengths, MODERNBERT_BASE.vocab, seed=5000 + rank)
+        spec, name, dtype = MODERNBERT_BASE, "modernbert_base_index_sweep", "bf16"
+        desc = f"{n_total} chunks total, log-normal median 180 sigma 0.8 clip [16,1024], sharded by token count"
+    else:
+        spec, name, dtype, desc, lengths, ids, cu = encoder_workload(args, rank)
+    tokens = int(cu[-1])
+    n = len(lengths)
+    w = synth.random_weights(spec, seed=1)
+    be = EmbedBackend(spec, w, dtype=dtype, device=local, max_batch_tokens=args.max_batch_tokens)
+    del w
+
+    stream = torch.cuda.current_stream()
+    ids_dev = torch.from_numpy(ids).cuda()
+    out_dev = torch.empty(n, spec.hidden, device="cuda", dtype=torch.float32)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        be.embed_device(ids_dev, cu, out_dev, stream=stream.cuda_stream)
+    barrier()
+
+    sampler = ClockSampler(physical_gpu(local))
+    sampler.start()
+    be._lib.rv_reset_profile(be._h)
+    be._lib.rv_set_profiling(be._h, 1)
+    launches0 = be.kernel_launches()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    for s in range(args.steps):
+        flush.zero_()  # L2 flush between timed steps (outside the events)
+        evs[s][0].record(stream)
+        be.embed_device(ids_dev, cu, out_dev, stream=stream.cuda_stream)
+        evs[s][1].record(stream)
+    barrier()
+    launches = be.kernel_launches() - launches0
+    be._lib.rv_set_profiling(be._h, 0)
+    clocks = sampler.stop()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    total_ms = max_over_ranks(sum(step_ms))
+    value = (tokens * args.steps * world) / (total_ms / 1e3)
+
+    prof = {}
+    import ctypes as C
+
+    for k, kname in enumerate(L.KIND_NAMES):
+        ms, cnt, fl = C.c_double(), C.c_int64(), C.c_double()
+        be._lib.rv_get_profile(be._h, k, C.byref(ms), C.byref(cnt), C.byref(fl))
+        prof[kname] = {"ms": ms.value, "launches": cnt.value, "flops": fl.value}
+    kern_total = sum(v["ms"] for v in prof.values()) or 1.0
+    pk = peaks()
+    g = prof["gemm_tc"]
+    gemm_ms_per_launch = g["ms"] / max(1, g["launches"])
+    gemm_flops_per_launch = g["flops"] / max(1, g["launches"])
+    achieved = gemm_flops_per_launch / (gemm_ms_per_launch / 1e3) / 1e12 if g["launches"] else 0.0
+    tpf = traffic_per_flop()
+    roofline = {"kernel": "gemm_tc (tcgen05 projection GEMMs, all four per layer)", "bound": "tensor",
+                "achieved": achieved, "peak": pk["bf16_sus"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_sus"],
+                "peak_source": f"{pk['source']} bf16_tflops_sustained (kernel timed inside a long step)",
+                "traffic": (tpf * gemm_flops_per_launch) if tpf else None,
+                "flops_per_launch": gemm_flops_per_launch, "ms_per_launch": gemm_ms_per_launch}
+    att = prof["attention_varlen"]
+    whole_flops = sum(v["flops"] for v in prof.values()) / args.steps
+    kernels = {k: {"ms_per_step": v["ms"] / args.steps, "share": v["ms"] / kern_total,
+                   "launches_per_step": v["launches"] / args.steps} for k, v in prof.items()}
+
+    # ---------------------------------------------------------------- e2e through the host API
+    e2e = None
+    if not args.no_e2e:
+        ids_h = torch.from_numpy(ids).pin_memory()
+        cu_h = np.ascontiguousarray(cu, np.int32)
+        out_h = torch.empty(n, spec.hidden, dtype=torch.float32).pin_memory()
+        ids_np = ids_h.numpy()
+        out_np = out_h.numpy()
+        for _ in range(max(1, min(args.warmup, 2))):
+            be.embed_packed(ids_np, cu_h, out_np)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            be.embed_packed(ids_np, cu_h, out_np)
+        torch.cuda.synchronize()
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+        nb = -(-tokens // args.max_batch_tokens) + 1
+        h2d = tokens * 4 + 8 * (n + nb)
+        e2e = {"value": tokens * args.steps * world / e2e_s, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(n * spec.hidden * 4),
+               "how": "rv_embed_varlen with pinned host ids / cu_seqlens / output, host clock around the synchronous call"}
+        if np.abs(np.linalg.norm(out_np, axis=1) - 1).max() > 1e-3:
+            raise RuntimeError("e2e outputs are not unit-norm")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("encoder", "long"):
+        w = synth.random_weights(spec, seed=1)
+        r, nc, tok, dt = cpu_encoder_rate(spec, w, lengths, ids, cu, 12.0)
+        cpu = {"value": r, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+               "sample": f"first {nc} chunks of the workload ({tok} tokens, {dt:.1f} s), numpy fp32 port of the reference CPU path"}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+                "scaling": "weak" if args.workload != "sweep" else "strong", "vs_baseline": None, "dtype": dtype,
+                "data": "synthetic (seeded random token ids, random-init N(0,0.02) weights)",
+                "config": {"workload": name, "model": "ModernBERT-base (22L, H768, 12x64, GeGLU 1152, window 128)",
+                           "chunks_per_gpu": n, "lengths": desc, "tokens_per_gpu": tokens,
+                           "global_batch": n * world, "seq_len": "varlen", "parallelism": f"dp{world}",
+                           "max_batch_tokens": args.max_batch_tokens, "l2": "flushed between steps (256 MiB write)"},
+                "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "cpu_baseline": cpu,
+                "clocks": clocks, "kernels": kernels,
+                "whole_step_tflops": whole_flops / (total_ms / args.steps / 1e3) / 1e12,
+                "attention_tflops": (att["flops"] / (att["ms"] / 1e3) / 1e12) if att["ms"] else None}
+        print(json.dumps(line), flush=True)
+    be.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_scan(args):
+    import ctypes as C
+
+    import torch
+
+    from ripvec_b200 import synth
+    from ripvec_b200.index import SearchIndex, merge_topk_device
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    n_rows, dim, nq, k = 10_000_000, 768, 1024, 100
+    lo, hi = rank * n_rows // world, (rank + 1) * n_rows // world
+    # shard rows generated on the device in blocks (normalised Gaussian, rounded to bf16 by the index)
+    gen = torch.Generator(device="cuda").manual_seed(100 + rank)
+    shard = torch.empty(hi - lo, dim, device="cuda", dtype=torch.bfloat16)
+    for s in range(0, hi - lo, 1 << 20):
+        e = min(hi - lo, s + (1 << 20))
+        x = torch.randn(e - s, dim, device="cuda", generator=gen)
+        shard[s:e] = (x / x.norm(dim=1, keepdim=True)).to(torch.bfloat16)
+    idx = SearchIndex(shard, device=local, base=lo)
+    del shard
+    q = torch.from_numpy(synth.normalized_gaussian(nq, dim, seed=99)).cuda()
+    oi = torch.empty(nq, k, dtype=torch.int64, device="cuda")
+    os_ = torch.empty(nq, k, dtype=torch.float32, device="cuda")
+    o64 = torch.empty(nq, k, dtype=torch.float64, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        idx.topk_device(q, k, oi, os_, o64, stream=stream.cuda_stream)
+        if dist is not None:
+            gi = [torch.empty_like(oi) for _ in range(world)]
+            gs = [torch.empty_like(o64) for _ in range(world)]
+            dist.all_gather(gi, oi)
+            dist.all_gather(gs, o64)
+            merge_topk_device(torch.stack(gi), torch.stack(gs), k, device=local, stream=stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for s in range(args.steps):
+        evs[s][0].record(stream)
+        step()
+        evs[s][1].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs)
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank == 0:
+        pk = peaks()
+        db_bytes = (n_rows // world) * dim * 2
+        line = {"metric": "exact cosine top-100 queries/sec (10M x 768 bf16)", "value": nq * args.steps / (ms / 1e3),
+                "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic normalised Gaussian rows",
+                "config": {"workload": "scan_topk", "rows": n_rows, "dim": dim, "queries": nq, "k": k,
+                           "parallelism": f"rows{world}"},
+                "db_gbs_per_rank": db_bytes / (ms / args.steps / 1e3) / 1e9, "hbm_peak_gbs": pk["hbm_gbs"]}
+        print(json.dumps(line), flush=True)
+    idx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.workload == "scan":
+        return run_scan(args)
+    return run_encoder(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,167 @@
+/*
+ * ripvec_b200 — C ABI of the B200 (sm_100a) embedding backend and cosine top-k scan.
+ *
+ * The library replaces, behind a thin FFI shim, the hot path of fnordpig/ripvec:
+ *   - the embedding backend (`EmbedBackend`, crates/ripvec-core/src/backend/mod.rs:49-94,
+ *     implemented for GPUs by `GenericBackend<CudaDriver, ModernBertArch>`,
+ *     backend/generic.rs:147-184, and for ClassicBert by backend/cpu.rs:722-748), and
+ *   - the exact search (`SearchIndex::new` / `SearchIndex::rank`,
+ *     crates/ripvec-core/src/index.rs:76-186, scoring `similarity::rank_all`,
+ *     similarity.rs:24-26).
+ *
+ * Conventions: every entry point returns 0 (RV_OK) on success or a negative RV_E* code; the
+ * message of the last failure on a handle is returned by rv_last_error / rv_index_last_error.
+ * Nothing aborts or exits.  Input pointers are not retained after a call returns.  Host buffers
+ * are plain CPU memory (pinned or not); "device" buffers are CUDA device pointers on the
+ * handle's device.  A context or index may be used from several threads: calls on one handle
+ * are serialised internally.
+ */
+#ifndef RIPVEC_B200_H
+#define RIPVEC_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status codes */
+#define RV_OK 0
+#define RV_E_INVALID -1     /* bad argument (null pointer, size, shape, unsupported option) */
+#define RV_E_CUDA -2        /* CUDA runtime error */
+#define RV_E_NOT_READY -3   /* weights missing / model not finalised */
+#define RV_E_IO -4          /* file could not be read or parsed */
+#define RV_E_DEVICE -5      /* a kernel reported an error (bounded wait expired, bad token) */
+#define RV_E_NOMEM -6       /* device allocation failed */
+
+/* ---------------------------------------------------------------- model description */
+#define RV_ARCH_MODERNBERT 1  /* backend/arch/modern_bert.rs */
+#define RV_ARCH_CLASSICBERT 2 /* backend/cpu.rs (BGE / BERT) */
+
+#define RV_DTYPE_F32 0
+#define RV_DTYPE_BF16 1
+#define RV_DTYPE_F16 2
+
+#define RV_POOL_MEAN 0 /* mean over the sequence (ModernBERT; BASELINE ClassicBert config) */
+#define RV_POOL_CLS 1  /* first token (the reference ClassicBert CPU backend) */
+
+/* Mirrors ModernBertConfig (backend/driver/cpu.rs:620-667) and BertConfig (backend/cpu.rs:52-92). */
+typedef struct rv_model_desc {
+  int32_t arch;                /* RV_ARCH_* */
+  int32_t dtype;               /* RV_DTYPE_BF16 or RV_DTYPE_F16: device storage of weights and activations */
+  int32_t hidden;              /* 768 (ModernBERT-base) / 384 (BERT-small) */
+  int32_t num_layers;          /* 22 / 12 */
+  int32_t num_heads;           /* 12 / 12 */
+  int32_t intermediate;        /* 1152 (GeGLU half width) / 1536 */
+  int32_t vocab;               /* 50368 / 30522 */
+  int32_t max_position;        /* 8192 / 512 */
+  int32_t global_every_n;      /* ModernBERT: layer i is global iff i % n == 0 (3) */
+  int32_t local_window;        /* ModernBERT: 128 (keys with |i-j| <= 64 are visible) */
+  float global_rope_theta;     /* 160000 */
+  float local_rope_theta;      /* 10000 */
+  float norm_eps;              /* 1e-5 / 1e-12 */
+  int32_t type_vocab;          /* ClassicBert token-type rows (2) */
+  int32_t pooling;             /* RV_POOL_MEAN / RV_POOL_CLS */
+  int64_t max_batch_tokens;    /* device workspace: packed tokens per forward (0 = 262144) */
+} rv_model_desc;
+
+typedef struct rv_ctx rv_ctx;
+
+/* Creates a context on CUDA device `device` for the model described by *desc.  Weights are then
+ * supplied with rv_set_weight (or rv_load_safetensors) and the model is frozen by rv_finalize. */
+int rv_create(const rv_model_desc* desc, int device, rv_ctx** out);
+void rv_destroy(rv_ctx* ctx);
+
+/* Uploads one named f32 host tensor (names as in the reference's safetensors files, e.g.
+ * "layers.3.attn.Wqkv.weight", "embeddings.tok_embeddings.weight", "final_norm.weight";
+ * ClassicBert: "encoder.layer.0.attention.self.query.weight", ...).  numel must match. */
+int rv_set_weight(rv_ctx* ctx, const char* name, const float* host, int64_t numel);
+/* Reads every tensor of a safetensors file (F32, BF16 or F16) through rv_set_weight. */
+int rv_load_safetensors(rv_ctx* ctx, const char* path);
+/* Checks that every weight is present and builds the device layouts (interleaved Wi, RoPE
+ * tables, TMA descriptors).  Required before rv_embed_*. */
+int rv_finalize(rv_ctx* ctx);
+
+/* EmbedBackend::embed_batch.  ids: packed int32 token ids of n_seqs sequences, sequence b being
+ * ids[cu_seqlens[b] .. cu_seqlens[b+1]); cu_seqlens has n_seqs+1 entries, cu_seqlens[0] = 0,
+ * non-decreasing, every length <= rv_max_tokens.  out_host: [n_seqs, hidden] f32 L2-normalised
+ * embeddings in input order.  Host buffers; the copies are part of the call. */
+int rv_embed_varlen(rv_ctx* ctx, const int32_t* ids, const int32_t* cu_seqlens, int32_t n_seqs,
+                    float* out_host);
+/* Same with device-resident ids and output (out_dev: [n_seqs, hidden] of out_dtype f32/bf16/f16);
+ * cu_seqlens stays on the host (it drives the token-budget packing).  stream may be 0. */
+int rv_embed_varlen_device(rv_ctx* ctx, const int32_t* ids_dev, const int32_t* cu_seqlens_host,
+                           int32_t n_seqs, void* out_dev, int32_t out_dtype, void* stream);
+
+int rv_max_tokens(const rv_ctx* ctx);   /* EmbedBackend::max_tokens */
+int rv_hidden_dim(const rv_ctx* ctx);
+const char* rv_name(const rv_ctx* ctx); /* EmbedBackend::name */
+int rv_is_gpu(const rv_ctx* ctx);       /* EmbedBackend::is_gpu (1) */
+const char* rv_last_error(const rv_ctx* ctx);
+/* Number of kernels this context launched since creation (for launch accounting). */
+int64_t rv_kernel_launches(const rv_ctx* ctx);
+
+/* Per-kernel timing: when enabled, every kernel launch of rv_embed_* is bracketed by CUDA events
+ * on the context's stream and its device time is accumulated per kernel kind. */
+#define RV_KIND_GEMM 0      /* tcgen05 projection GEMMs (all four per layer) */
+#define RV_KIND_ATTENTION 1 /* varlen attention */
+#define RV_KIND_NORM 2      /* LayerNorm */
+#define RV_KIND_EMBED 3     /* embedding gather + LayerNorm, positions */
+#define RV_KIND_POOL 4      /* final LayerNorm + mean pool + L2 */
+#define RV_KIND_COUNT 5
+int rv_set_profiling(rv_ctx* ctx, int enable);
+/* Totals since the last reset: device milliseconds, launches and algorithmic FLOPs (GEMM: 2MNK;
+ * attention: 4 * head_dim * heads * visible query-key pairs; others 0). */
+int rv_get_profile(rv_ctx* ctx, int kind, double* total_ms, int64_t* launches, double* flops);
+int rv_reset_profile(rv_ctx* ctx);
+
+/* ---------------------------------------------------------------- search */
+typedef struct rv_index rv_index;
+
+/* SearchIndex::new: a bf16 device copy of n rows of dimension dim.  src is f32, bf16 or f16
+ * (src_dtype); src_on_device selects a device or host source.  Rows are stored as given (the
+ * reference stores embed_batch output, already L2-normalised). */
+int rv_index_create(int device, const void* src, int64_t n, int32_t dim, int32_t src_dtype,
+                    int32_t src_on_device, rv_index** out);
+void rv_index_destroy(rv_index* idx);
+const char* rv_index_last_error(const rv_index* idx);
+int64_t rv_index_size(const rv_index* idx);
+/* Global row index of this shard's first row (rows are numbered base + local row in results). */
+int rv_index_set_base(rv_index* idx, int64_t base);
+
+/* SearchIndex::rank restricted to the best k: for each of nq queries (f32, [nq, dim], rounded
+ * to bf16 like the stored rows) return its k best rows ordered by (score desc, row asc), scores
+ * computed exactly (sequential f64 sum of exact bf16 products).  Rows scoring below threshold
+ * are dropped: out_count[q] (optional) receives the number kept and the tail of out_idx is
+ * filled with -1 / out_score with -inf.  out_idx [nq, k] int64, out_score [nq, k] f32; the f64
+ * scores are also returned when out_score64 is non-null.  Host buffers. */
+int rv_index_topk(rv_index* idx, const float* queries, int32_t nq, int32_t k, float threshold,
+                  int64_t* out_idx, float* out_score, double* out_score64, int32_t* out_count);
+/* Device-buffer variant of rv_index_topk (queries_dev f32 [nq, dim]; outputs on the device). */
+int rv_index_topk_device(rv_index* idx, const float* queries_dev, int32_t nq, int32_t k,
+                         float threshold, int64_t* out_idx_dev, float* out_score_dev,
+                         double* out_score64_dev, void* stream);
+/* Merges n_lists per-shard results [n_lists, nq, k] (device; idx int64, score f64, as returned
+ * by rv_index_topk_device) into the global top k per query, ordered by (score desc, idx asc). */
+int rv_topk_merge_device(int device, const int64_t* idx_in, const double* score_in,
+                         int32_t n_lists, int32_t nq, int32_t k, float threshold,
+                         int64_t* idx_out, float* score_out, double* score64_out, void* stream);
+
+/* ---------------------------------------------------------------- single-kernel entry points
+ * Used by the parity tests to check one kernel against the CPU oracle.  Device pointers. */
+/* C[M,N] (f32 or act) = A[M,K] B[N,K]^T with A, B of act dtype (RV_DTYPE_BF16/F16). */
+int rv_op_gemm(int32_t act_dtype, const void* a, const void* b, void* c, int32_t c_dtype,
+               int32_t M, int32_t N, int32_t K, int32_t bn, void* stream);
+/* Attention over packed qkv [T, 3*heads*head_dim]; window_half < 0 = global. */
+int rv_op_attention(int32_t act_dtype, const void* qkv, void* ctx_out, const int32_t* cu_seqlens_host,
+                    int32_t n_seqs, int32_t num_heads, int32_t head_dim, int32_t window_half,
+                    float scale, void* stream);
+/* out = LN(in) * gamma (+ beta); 16-bit rows. */
+int rv_op_layernorm(int32_t act_dtype, const void* in, void* out, int32_t rows, int32_t hidden,
+                    const float* gamma, const float* beta, float eps, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RIPVEC_B200_H */

@@ -1,0 +1,119 @@
+"""Exact cosine ranking — restatement of the reference search path.
+
+TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).
+
+``rank`` follows ``SearchIndex::rank`` (``crates/ripvec-core/src/index.rs:172-186``): a dimension
+check (wrong or empty query -> no results), scores ``embeddings @ query`` (``similarity.rs:24-26``),
+``score >= threshold`` filter, sort by descending score.  The reference's ``sort_unstable_by``
+leaves the order of equal scores unspecified; this build fixes it to (score desc, row asc), the
+order ``rrf_fuse`` uses (``hybrid.rs:198-200``).
+
+``topk_exact`` is the bit-exact definition the GPU scan is checked against: rows and query are
+bf16 values, each score is the sequential sum over d = 0..dim-1 in float64 of the (exact)
+bf16 x bf16 products, results are ordered by (score desc, row asc), the best k are kept, and
+rows scoring below ``threshold`` are dropped after selection.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import ops
+
+
+def dot_product(a, b) -> float:
+    """``similarity::dot_product`` (``similarity.rs:12-15``)."""
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    s = np.float32(0.0)
+    for x, y in zip(a, b):
+        s = np.float32(s + np.float32(x * y))
+    return float(s)
+
+
+def rank_all(embeddings: np.ndarray, query: np.ndarray) -> np.ndarray:
+    """``similarity::rank_all``: ``embeddings @ query`` in f32 (``similarity.rs:24-26``)."""
+    embeddings = np.asarray(embeddings, np.float32)
+    if embeddings.shape[0] == 0:
+        return np.zeros(0, np.float32)
+    return embeddings @ np.asarray(query, np.float32)
+
+
+def rank(embeddings: np.ndarray, query, threshold: float) -> list[tuple[int, float]]:
+    """``SearchIndex::rank`` (``index.rs:172-186``) with the (score desc, row asc) tie order."""
+    embeddings = np.asarray(embeddings, np.float32)
+    query = np.asarray(query, np.float32)
+    if embeddings.ndim != 2 or query.shape != (embeddings.shape[1],) or embeddings.shape[0] == 0:
+        return []
+    s = rank_all(embeddings, query)
+    keep = np.nonzero(s >= np.float32(threshold))[0]
+    order = np.lexsort((keep, -s[keep].astype(np.float64)))
+    return [(int(keep[i]), float(s[keep[i]])) for i in order]
+
+
+def scores_exact(db_bf16: np.ndarray, q_bf16: np.ndarray) -> np.ndarray:
+    """Float64 scores of every row, summing d = 0..dim-1 in order (products are exact in f64)."""
+    db = np.asarray(db_bf16, np.float64)
+    q = np.asarray(q_bf16, np.float64)
+    acc = np.zeros(db.shape[0], np.float64)
+    for d in range(db.shape[1]):
+        acc += db[:, d] * q[d]
+    return acc
+
+
+def topk_exact(db: np.ndarray, queries: np.ndarray, k: int, threshold: float = -np.inf):
+    """Reference top-k of every query: returns ``(idx int64 [nq,k], score64 [nq,k], count [nq])``.
+
+    ``db`` and ``queries`` are rounded to bf16 first (the GPU index stores bf16 rows and rounds
+    the f32 queries the same way).  Missing entries are ``-1`` / ``-inf``.
+    """
+    dbb = ops.to_bf16(np.asarray(db, np.float32))
+    qb = ops.to_bf16(np.asarray(queries, np.float32).reshape(-1, dbb.shape[1]))
+    nq, n = qb.shape[0], dbb.shape[0]
+    out_i = np.full((nq, k), -1, np.int64)
+    out_s = np.full((nq, k), -np.inf, np.float64)
+    cnt = np.zeros(nq, np.int32)
+    kk = min(k, n)
+    if kk == 0 or nq == 0:
+        return out_i, out_s, cnt
+    # Sequential f64 sums over d for all queries at once, in row blocks (the order of the
+    # additions per (query, row) is d = 0, 1, ..., dim-1, as in scores_exact).
+    q64 = qb.astype(np.float64)
+    best_i = [np.zeros(0, np.int64) for _ in range(nq)]
+    best_s = [np.zeros(0, np.float64) for _ in range(nq)]
+    step = max(1, (1 << 22) // max(nq, 1))
+    for r0 in range(0, n, step):
+        blk = dbb[r0:r0 + step].astype(np.float64)
+        acc = np.zeros((nq, blk.shape[0]), np.float64)
+        for d in range(blk.shape[1]):
+            acc += q64[:, d:d + 1] * blk[None, :, d]
+        rows = np.arange(r0, r0 + blk.shape[0], dtype=np.int64)
+        for qi in range(nq):
+            ii = np.concatenate([best_i[qi], rows])
+            ss = np.concatenate([best_s[qi], acc[qi]])
+            order = np.lexsort((ii, -ss))[:kk]
+            best_i[qi], best_s[qi] = ii[order], ss[order]
+    for qi in range(nq):
+        sel = best_s[qi] >= threshold
+        c = int(sel.sum())
+        out_i[qi, :c] = best_i[qi][sel]
+        out_s[qi, :c] = best_s[qi][sel]
+        cnt[qi] = c
+    return out_i, out_s, cnt
+
+
+def merge_topk(idx_lists: np.ndarray, score_lists: np.ndarray, k: int, threshold: float = -np.inf):
+    """Merge per-shard results ``[n_lists, nq, k]`` into the global best k by (score desc, idx asc)."""
+    n_lists, nq, kk = idx_lists.shape
+    out_i = np.full((nq, k), -1, np.int64)
+    out_s = np.full((nq, k), -np.inf, np.float64)
+    for q in range(nq):
+        ii = idx_lists[:, q, :].reshape(-1)
+        ss = score_lists[:, q, :].reshape(-1)
+        valid = ii >= 0
+        ii, ss = ii[valid], ss[valid]
+        order = np.lexsort((ii, -ss))[:k]
+        order = order[ss[order] >= threshold]
+        out_i[q, :len(order)] = ii[order]
+        out_s[q, :len(order)] = ss[order]
+    return out_i, out_s

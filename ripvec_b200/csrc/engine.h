@@ -1,0 +1,103 @@
+// Host-side engine shared by the C ABI translation units: the context object, weight storage,
+// workspaces and small utilities.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/ripvec_b200.h"
+#include "kernels.h"
+
+namespace rv {
+
+// Rounds f32 to bf16 (round to nearest even), host side.
+uint16_t f32_to_bf16_bits(float f);
+uint16_t f32_to_f16_bits(float f);
+
+// Converts host f32 to the device dtype and uploads.  Returns false on CUDA error.
+bool upload_converted(const float* host, int64_t n, Act act, void** dev, std::string* why);
+bool upload_f32(const float* host, int64_t n, float** dev, std::string* why);
+
+struct DeviceMatrix {
+  void* ptr = nullptr;   // [rows, cols] 16-bit, row-major
+  int rows = 0, cols = 0;
+  CUtensorMap tmap;      // B-operand map, box 64 x bn
+  int bn = 256;
+};
+
+struct LayerWeights {
+  DeviceMatrix wqkv, wo, wi, wo2;
+  float* attn_norm = nullptr;  // ModernBERT (null for layer 0)
+  float* mlp_norm = nullptr;
+  float* bqkv = nullptr;       // ClassicBert biases and post-LN parameters
+  float* bo = nullptr;
+  float* ln1_w = nullptr;
+  float* ln1_b = nullptr;
+  float* b1 = nullptr;
+  float* b2 = nullptr;
+  float* ln2_w = nullptr;
+  float* ln2_b = nullptr;
+  bool is_global = true;
+};
+
+}  // namespace rv
+
+struct rv_ctx {
+  rv_model_desc d{};
+  int device = 0;
+  rv::Act adt = rv::Act::kBf16;  // device storage dtype
+  std::mutex mu;
+  std::string err;
+  cudaStream_t stream = nullptr;
+  unsigned int* d_err = nullptr;
+  int64_t launches = 0;
+  bool finalized = false;
+  std::map<std::string, std::vector<float>> host_w;  // staged until rv_finalize
+
+  // device weights
+  float* tok_emb = nullptr;     // [vocab, hidden] f32
+  float* emb_norm_w = nullptr;
+  float* emb_norm_b = nullptr;  // ClassicBert
+  float* final_norm = nullptr;  // ModernBERT
+  float* pos_emb = nullptr;     // ClassicBert [max_position, hidden]
+  float* type_emb = nullptr;    // ClassicBert [type_vocab, hidden]
+  float* rope_cos[2] = {nullptr, nullptr};  // [0] global theta, [1] local theta; [max_pos, 32]
+  float* rope_sin[2] = {nullptr, nullptr};
+  std::vector<rv::LayerWeights> layers;
+
+  // workspaces
+  int64_t t_max = 0;
+  int n_max = 0;
+  void* x = nullptr;    // residual stream [t_max, hidden]
+  void* hn = nullptr;   // normalised input of the next projection
+  void* qkv = nullptr;  // [t_max, 3*hidden]
+  void* cbuf = nullptr; // attention context [t_max, hidden]
+  void* act = nullptr;  // MLP activation [t_max, intermediate]
+  int* ids_d = nullptr;
+  int* pos_d = nullptr;
+  int* meta_d = nullptr;  // cu_seqlens (n_max+1) then q-tile starts (n_max+1)
+  float* out_d = nullptr; // [n_max, hidden]
+  int* meta_h = nullptr;  // pinned staging of meta_d
+  cudaEvent_t meta_evt = nullptr;
+  CUtensorMap map_x, map_hn, map_c, map_act;
+
+  std::vector<void*> allocations;
+
+  // per-kernel profiling (rv_set_profiling)
+  bool profiling = false;
+  struct Mark {
+    int kind;
+    cudaEvent_t a, b;
+    double flops;
+  };
+  std::vector<Mark> marks;            // recorded, not yet read
+  std::vector<cudaEvent_t> ev_pool;   // free events
+  double prof_ms[RV_KIND_COUNT] = {0};
+  int64_t prof_n[RV_KIND_COUNT] = {0};
+  double prof_flops[RV_KIND_COUNT] = {0};
+};

@@ -1,0 +1,357 @@
+// C ABI of the search side: a bf16 device copy of the embedding matrix (SearchIndex::new,
+// crates/ripvec-core/src/index.rs:76-165) and the exact cosine top-k (SearchIndex::rank,
+// index.rs:172-186, restricted to the best k with the (score desc, row asc) order).
+#include <cuda_bf16.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/ripvec_b200.h"
+#include "engine.h"
+#include "kernels.h"
+#include "scan.h"
+#include "tmap.h"
+
+template <typename T>
+struct DevBuf {
+  T* p = nullptr;
+  size_t cap = 0;
+  // Ensures room for `need` elements (contents are not preserved).  False on allocation failure.
+  bool reserve(size_t need) {
+    if (p && cap >= need) return true;
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+    if (cudaMalloc(reinterpret_cast<void**>(&p), (need ? need : 1) * sizeof(T)) != cudaSuccess) return false;
+    cap = need;
+    return true;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+  }
+};
+
+struct rv_index {
+  int device = 0;
+  std::mutex mu;
+  std::string err;
+  cudaStream_t stream = nullptr;
+  __nv_bfloat16* db = nullptr;
+  int64_t n = 0;
+  int dim = 0;
+  int64_t base = 0;
+  double max_norm = 0.0;
+  CUtensorMap tmap_db;
+  unsigned int* d_err = nullptr;
+  // scratch, grown on demand
+  DevBuf<float> scores, qf, list_s, os;
+  DevBuf<__nv_bfloat16> qb;
+  DevBuf<int64_t> list_i, oi;
+  DevBuf<int> list_n, cnt, guard;
+  DevBuf<double> os64;
+  int64_t launches = 0;
+};
+
+namespace {
+
+int ifail(rv_index* x, int code, const std::string& m) {
+  if (x) x->err = m;
+  return code;
+}
+
+#define IX_TRY(x, expr)                                                                  \
+  do {                                                                                   \
+    cudaError_t _e = (expr);                                                             \
+    if (_e != cudaSuccess)                                                               \
+      return ifail(x, RV_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e));    \
+  } while (0)
+
+struct Dev {
+  int prev = -1;
+  explicit Dev(int d) {
+    cudaGetDevice(&prev);
+    if (prev != d) cudaSetDevice(d);
+  }
+  ~Dev() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// Runs one query batch end to end on x->stream for candidate width kp.
+int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int k, int kp, float threshold,
+              int64_t* out_i, float* out_s, double* out_s64) {
+  cudaStream_t st = x->stream;
+  if (!x->list_s.reserve(size_t(nq) * kp) || !x->list_i.reserve(size_t(nq) * kp) ||
+      !x->list_n.reserve(size_t(nq)))
+    return ifail(x, RV_E_NOMEM, "scan list allocation failed");
+  IX_TRY(x, rv::scan_init_lists(x->list_n.p, nq, st));
+  x->launches++;
+  const int cap = rv::scan_cap_for(kp);
+  if (x->n > 0) {
+    CUtensorMap tq;
+    std::string why;
+    if (!rv::make_tmap_2d_16bit(&tq, qb, true, x->dim, nq, uint64_t(x->dim) * 2, 64, 128, &why))
+      return ifail(x, RV_E_CUDA, why);
+    // Chunk schedule: the first chunk fits the select buffer with an empty list; later chunks
+    // grow with the rows already seen so the expected number of survivors stays well below
+    // the buffer; S = [nq, chunk] f32 is kept near 32 MB so it stays in L2.
+    int64_t cmax = (int64_t(32) << 20) / (int64_t(nq) * 4);
+    cmax = std::max<int64_t>(256, std::min<int64_t>(cmax, int64_t(1) << 22)) / 256 * 256;
+    if (!x->scores.reserve(size_t(nq) * size_t(cmax)))
+      return ifail(x, RV_E_NOMEM, "scan score buffer allocation failed");
+    int64_t r0 = 0;
+    int64_t chunk = std::max<int64_t>(256, (cap - kp) / 256 * 256);
+    while (r0 < x->n) {
+      const int64_t valid = std::min<int64_t>(chunk, x->n - r0);
+      const int64_t ncols = (valid + 255) / 256 * 256;
+      rv::GemmArgs g{};
+      g.tmA = &tq;
+      g.tmB = &x->tmap_db;
+      g.M = nq;
+      g.N = static_cast<int>(ncols);
+      g.K = x->dim;
+      g.bn = 256;
+      g.b_row_offset = static_cast<int>(r0);
+      g.epi = rv::GemmEpi::kStoreF32;
+      g.c = x->scores.p;
+      g.ldc = static_cast<int>(ncols);
+      IX_TRY(x, rv::gemm_tc(rv::Act::kBf16, g, x->d_err, st));
+      IX_TRY(x, rv::scan_select(x->scores.p, static_cast<int>(ncols), static_cast<int>(valid),
+                                x->base + r0, nq, kp, x->list_s.p, x->list_i.p, x->list_n.p, st));
+      x->launches += 2;
+      r0 += valid;
+      const int64_t grow_to = (int64_t(cap - kp) * r0) / (4 * int64_t(kp));
+      chunk = std::max<int64_t>(256, std::min<int64_t>(cmax, grow_to) / 256 * 256);
+    }
+  }
+  if (!x->cnt.reserve(size_t(nq)) || !x->guard.reserve(size_t(nq)))
+    return ifail(x, RV_E_NOMEM, "scan output allocation failed");
+  const double eps_scale = double(x->dim) * std::ldexp(1.0, -22) * x->max_norm;
+  IX_TRY(x, rv::scan_rescore(x->db, x->base, x->dim, qb, nq, x->list_s.p, x->list_i.p, x->list_n.p,
+                             kp, k, x->n, eps_scale, threshold, out_i, out_s, out_s64, x->cnt.p,
+                             x->guard.p, st));
+  x->launches++;
+  return RV_OK;
+}
+
+int topk_device(rv_index* x, const float* q_dev, int nq, int k, float threshold, int64_t* out_i,
+                float* out_s, double* out_s64, std::vector<int>* counts) {
+  if (nq <= 0) return RV_OK;
+  if (k <= 0 || k > 2048) return ifail(x, RV_E_INVALID, "k must be in [1, 2048]");
+  cudaStream_t st = x->stream;
+  if (!x->qb.reserve(size_t(nq) * x->dim)) return ifail(x, RV_E_NOMEM, "query buffer");
+  IX_TRY(x, rv::scan_round_queries(q_dev, x->qb.p, int64_t(nq) * x->dim, st));
+  x->launches++;
+  int kp = std::max(128, 2 * k);
+  for (;;) {
+    int rc = topk_pass(x, x->qb.p, nq, k, kp, threshold, out_i, out_s, out_s64);
+    if (rc) return rc;
+    std::vector<int> g(nq);
+    unsigned int e = 0;
+    IX_TRY(x, cudaMemcpyAsync(g.data(), x->guard.p, sizeof(int) * nq, cudaMemcpyDeviceToHost, st));
+    IX_TRY(x, cudaMemcpyAsync(&e, x->d_err, 4, cudaMemcpyDeviceToHost, st));
+    if (counts) {
+      counts->resize(nq);
+      IX_TRY(x, cudaMemcpyAsync(counts->data(), x->cnt.p, sizeof(int) * nq, cudaMemcpyDeviceToHost, st));
+    }
+    IX_TRY(x, cudaStreamSynchronize(st));
+    if (e) {
+      cudaMemset(x->d_err, 0, 4);
+      return ifail(x, RV_E_DEVICE, "scan kernel reported device error flags " + std::to_string(e));
+    }
+    bool any = false;
+    for (int v : g) any |= (v != 0);
+    if (!any) return RV_OK;
+    if (kp >= 4096)
+      return ifail(x, RV_E_DEVICE,
+                   "exact top-k needs more than 4096 candidates (too many near-equal scores)");
+    kp = std::min(4096, kp * 4);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int rv_index_create(int device, const void* src, int64_t n, int32_t dim, int32_t src_dtype,
+                    int32_t src_on_device, rv_index** out) {
+  if (!out) return RV_E_INVALID;
+  *out = nullptr;
+  if (n < 0 || dim <= 0 || dim % 64 != 0 || dim > 8192 || (n > 0 && !src)) return RV_E_INVALID;
+  if (src_dtype != RV_DTYPE_F32 && src_dtype != RV_DTYPE_BF16) return RV_E_INVALID;
+  if (n > (int64_t(1) << 31) - 1) return RV_E_INVALID;
+  Dev g(device);
+  rv_index* x = new rv_index();
+  x->device = device;
+  x->n = n;
+  x->dim = dim;
+  auto bail = [&](int code) {
+    rv_index_destroy(x);
+    return code;
+  };
+  if (cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking) != cudaSuccess) return bail(RV_E_CUDA);
+  if (cudaMalloc(&x->d_err, 4) != cudaSuccess || cudaMemset(x->d_err, 0, 4) != cudaSuccess)
+    return bail(RV_E_NOMEM);
+  const size_t elems = size_t(n) * dim;
+  if (n > 0 && cudaMalloc(&x->db, elems * 2) != cudaSuccess) return bail(RV_E_NOMEM);
+  if (n > 0) {
+    if (src_on_device) {
+      if (src_dtype == RV_DTYPE_BF16) {
+        if (cudaMemcpyAsync(x->db, src, elems * 2, cudaMemcpyDeviceToDevice, x->stream) != cudaSuccess)
+          return bail(RV_E_CUDA);
+      } else if (rv::scan_round_queries(static_cast<const float*>(src), x->db, int64_t(elems),
+                                        x->stream) != cudaSuccess) {
+        return bail(RV_E_CUDA);
+      }
+    } else {
+      const size_t chunk = size_t(1) << 24;
+      std::vector<uint16_t> tmp;
+      for (size_t s = 0; s < elems; s += chunk) {
+        const size_t e = std::min(elems, s + chunk);
+        const void* from;
+        if (src_dtype == RV_DTYPE_F32) {
+          tmp.resize(e - s);
+          const float* f = static_cast<const float*>(src);
+          for (size_t i = s; i < e; ++i) tmp[i - s] = rv::f32_to_bf16_bits(f[i]);
+          from = tmp.data();
+        } else {
+          from = static_cast<const uint16_t*>(src) + s;
+        }
+        if (cudaMemcpy(x->db + s, from, (e - s) * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+          return bail(RV_E_CUDA);
+      }
+    }
+    unsigned int* mx = nullptr;
+    unsigned int hmx = 0;
+    if (cudaMalloc(&mx, 4) != cudaSuccess) return bail(RV_E_NOMEM);
+    cudaMemsetAsync(mx, 0, 4, x->stream);
+    rv::scan_row_norm_max(x->db, n, dim, mx, x->stream);
+    cudaMemcpyAsync(&hmx, mx, 4, cudaMemcpyDeviceToHost, x->stream);
+    if (cudaStreamSynchronize(x->stream) != cudaSuccess) {
+      cudaFree(mx);
+      return bail(RV_E_CUDA);
+    }
+    cudaFree(mx);
+    float m2;
+    std::memcpy(&m2, &hmx, 4);
+    // Norm from the f32 sum of squares, widened by a relative 1e-3 for its rounding.
+    x->max_norm = std::sqrt(double(m2)) * 1.001 + 1e-30;
+    std::string why;
+    if (!rv::make_tmap_2d_16bit(&x->tmap_db, x->db, true, dim, n, uint64_t(dim) * 2, 64, 256, &why)) {
+      x->err = why;
+      return bail(RV_E_CUDA);
+    }
+  }
+  *out = x;
+  return RV_OK;
+}
+
+void rv_index_destroy(rv_index* x) {
+  if (!x) return;
+  {
+    Dev g(x->device);
+    if (x->stream) cudaStreamSynchronize(x->stream);
+    if (x->db) cudaFree(x->db);
+    if (x->d_err) cudaFree(x->d_err);
+    x->scores.release();
+    x->qf.release();
+    x->list_s.release();
+    x->os.release();
+    x->qb.release();
+    x->list_i.release();
+    x->oi.release();
+    x->list_n.release();
+    x->cnt.release();
+    x->guard.release();
+    x->os64.release();
+    if (x->stream) cudaStreamDestroy(x->stream);
+  }
+  delete x;
+}
+
+const char* rv_index_last_error(const rv_index* x) { return x ? x->err.c_str() : "null index"; }
+int64_t rv_index_size(const rv_index* x) { return x ? x->n : 0; }
+int rv_index_set_base(rv_index* x, int64_t base) {
+  if (!x || base < 0) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  x->base = base;
+  return RV_OK;
+}
+
+int rv_index_topk_device(rv_index* x, const float* q_dev, int32_t nq, int32_t k, float threshold,
+                         int64_t* out_i, float* out_s, double* out_s64, void* stream) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (nq < 0 || (nq > 0 && (!q_dev || !out_i || !out_s))) return ifail(x, RV_E_INVALID, "null argument");
+  Dev g(x->device);
+  cudaStream_t user = static_cast<cudaStream_t>(stream);
+  cudaEvent_t ev = nullptr;
+  if (user) {
+    IX_TRY(x, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    IX_TRY(x, cudaEventRecord(ev, user));
+    IX_TRY(x, cudaStreamWaitEvent(x->stream, ev, 0));
+  }
+  int rc = topk_device(x, q_dev, nq, k, threshold, out_i, out_s, out_s64, nullptr);
+  if (ev) {
+    if (rc == RV_OK) {
+      cudaEventRecord(ev, x->stream);
+      cudaStreamWaitEvent(user, ev, 0);
+    }
+    cudaEventDestroy(ev);
+  }
+  return rc;
+}
+
+int rv_index_topk(rv_index* x, const float* queries, int32_t nq, int32_t k, float threshold,
+                  int64_t* out_idx, float* out_score, double* out_score64, int32_t* out_count) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (nq < 0 || (nq > 0 && (!queries || !out_idx || !out_score)))
+    return ifail(x, RV_E_INVALID, "null argument");
+  if (nq == 0) return RV_OK;
+  if (k <= 0 || k > 2048) return ifail(x, RV_E_INVALID, "k must be in [1, 2048]");
+  Dev g(x->device);
+  cudaStream_t st = x->stream;
+  const size_t nk = size_t(nq) * k;
+  if (!x->qf.reserve(size_t(nq) * x->dim) || !x->oi.reserve(nk) || !x->os.reserve(nk) ||
+      (out_score64 && !x->os64.reserve(nk)))
+    return ifail(x, RV_E_NOMEM, "topk buffers");
+  IX_TRY(x, cudaMemcpyAsync(x->qf.p, queries, sizeof(float) * size_t(nq) * x->dim,
+                            cudaMemcpyHostToDevice, st));
+  std::vector<int> counts;
+  int rc = topk_device(x, x->qf.p, nq, k, threshold, x->oi.p, x->os.p,
+                       out_score64 ? x->os64.p : nullptr, &counts);
+  if (rc) return rc;
+  IX_TRY(x, cudaMemcpyAsync(out_idx, x->oi.p, sizeof(int64_t) * nk, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaMemcpyAsync(out_score, x->os.p, sizeof(float) * nk, cudaMemcpyDeviceToHost, st));
+  if (out_score64)
+    IX_TRY(x, cudaMemcpyAsync(out_score64, x->os64.p, sizeof(double) * nk, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaStreamSynchronize(st));
+  if (out_count)
+    for (int q = 0; q < nq; ++q) out_count[q] = counts[q];
+  return RV_OK;
+}
+
+int rv_topk_merge_device(int device, const int64_t* idx_in, const double* score_in, int32_t n_lists,
+                         int32_t nq, int32_t k, float threshold, int64_t* idx_out, float* score_out,
+                         double* score64_out, void* stream) {
+  if (n_lists <= 0 || nq < 0 || k <= 0 || !idx_in || !score_in || !idx_out || !score_out)
+    return RV_E_INVALID;
+  if (int64_t(n_lists) * k > 8192) return RV_E_INVALID;
+  if (nq == 0) return RV_OK;
+  Dev g(device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rv::scan_merge(idx_in, score_in, n_lists, nq, k, threshold, idx_out, score_out, score64_out, st) !=
+      cudaSuccess)
+    return RV_E_CUDA;
+  return cudaStreamSynchronize(st) == cudaSuccess ? RV_OK : RV_E_CUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,80 @@
+// Host-callable launchers of the sm_100a kernels (definitions in the .cu files).  All device
+// pointers; every launcher returns the launch status and never synchronizes.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rv {
+
+// Error bits written to a device error word by kernels that give up.
+enum DeviceError : unsigned int {
+  kErrWaitTimeout = 1u << 0,   // an mbarrier wait ran past its cycle limit
+  kErrBadShape = 1u << 1,      // a kernel saw an input it does not support (token id range)
+  kErrScanOverflow = 1u << 2,  // a candidate buffer of the top-k scan filled up
+};
+
+enum class Act { kBf16 = 0, kF16 = 1 };
+
+// Which epilogue a projection GEMM runs.
+enum class GemmEpi {
+  kStore = 0,      // C = A B^T
+  kResidual = 1,   // C += A B^T (+ bias)
+  kGeglu = 2,      // out = gelu(value) * gate over an interleaved Wi
+  kQkvRope = 3,    // C = A B^T, rotary embedding on the first rope_cols columns
+  kBias = 4,       // C = A B^T + bias
+  kBiasGelu = 5,   // C = gelu(A B^T + bias)
+  kStoreF32 = 6,   // C(f32) = A B^T
+};
+
+struct GemmArgs {
+  const CUtensorMap* tmA;  // A [M,K] K-major, box 64 x 128
+  const CUtensorMap* tmB;  // B [N,K] K-major, box 64 x BN
+  int M, N, K;
+  int bn;                  // 128 or 256 (N % bn == 0)
+  int b_row_offset;        // added to the B-operand row coordinate (chunked scans)
+  GemmEpi epi;
+  void* c;                 // output (or in/out for kResidual)
+  int ldc;                 // elements
+  const float* bias;       // kResidual / kBias / kBiasGelu (may be null)
+  int rope_cols;           // kQkvRope
+  const int* pos;          // kQkvRope: [M] position inside the sequence
+  const float* cos_t;      // kQkvRope: [max_pos, 32]
+  const float* sin_t;
+};
+
+cudaError_t gemm_tc(Act act, const GemmArgs& a, unsigned int* err, cudaStream_t st);
+
+// pos[t] = t - cu_seqlens[seq(t)] for t < total (binary search over cu_seqlens[0..n]).
+cudaError_t build_positions(const int* cu_seqlens, int n_seqs, int total, int* pos,
+                            cudaStream_t st);
+
+// ModernBERT embedding + LayerNorm: out[t] = LN(table_f32[ids[t]]) * gamma.
+cudaError_t embed_ln(Act act, const int* ids, int total, const float* table, int vocab,
+                     const float* gamma, const float* beta, const float* pos_table,
+                     const int* pos, const float* type_row, int hidden, float eps, void* out,
+                     unsigned int* err, cudaStream_t st);
+
+// out[t] = LN(in[t]) * gamma (+ beta), f32 statistics, 16-bit in/out.
+cudaError_t layernorm(Act act, const void* in, void* out, int rows, int hidden,
+                      const float* gamma, const float* beta, float eps, cudaStream_t st);
+
+// Pooling: mode 0 = final LN then mean over the sequence, 1 = mean (no LN), 2 = first token.
+// Then L2 normalisation: x / max(norm, l2_floor) when l2_floor > 0, else x / norm if norm > 0.
+cudaError_t pool_l2(Act act, const void* hidden_states, const int* cu_seqlens, int n_seqs,
+                    int hidden, int mode, const float* gamma, float eps, float l2_floor,
+                    float* out, cudaStream_t st);
+
+// Varlen bidirectional attention over packed qkv [T, 3*H] (Q | K | V, head h at h*D).
+// window_half < 0: global; else key j is visible from query i iff |i - j| <= window_half.
+// q_tile_starts[b] = first 64-query tile of sequence b (prefix sum of ceil(L_b/64)), n+1 entries.
+cudaError_t attention_varlen(Act act, const void* qkv, void* ctx, const int* cu_seqlens,
+                             const int* q_tile_starts, int n_seqs, int total_q_tiles,
+                             int num_heads, int head_dim, int window_half, float scale,
+                             cudaStream_t st);
+
+// f32 -> 16-bit conversion (weights upload), n elements.
+cudaError_t convert_f32(Act act, const float* in, void* out, int64_t n, cudaStream_t st);
+
+}  // namespace rv

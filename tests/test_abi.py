@@ -1,0 +1,68 @@
+"""The C ABI library loads on a machine without a GPU and exports every symbol the public header
+declares (no compute calls are made here)."""
+
+import re
+from pathlib import Path
+
+import pytest
+
+from ripvec_b200 import _lib
+from ripvec_b200.build import LIB, build
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "ripvec_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(rv_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()  # no-op when up to date; nvcc cross-compiles for sm_100a without a GPU
+    assert LIB.exists()
+    return _lib.lib()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    syms = declared_symbols()
+    assert len(syms) >= 20
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_binding_table_covers_the_header():
+    assert sorted(_lib.SIGNATURES) == declared_symbols()
+
+
+def test_null_arguments_are_rejected_without_a_device(lib):
+    import ctypes as C
+
+    assert lib.rv_create(None, 0, None) == _lib.RV_E_INVALID
+    assert lib.rv_index_create(0, None, 0, 63, _lib.RV_DTYPE_F32, 0, C.byref(C.c_void_p())) == _lib.RV_E_INVALID
+    d = _lib.ModelDesc()
+    d.arch = 99
+    assert lib.rv_create(C.byref(d), 0, C.byref(C.c_void_p())) == _lib.RV_E_INVALID
+    assert lib.rv_last_error(None) == b"null context"
+
+
+def test_model_desc_layout_matches_header(tmp_path):
+    """The ctypes mirror of rv_model_desc has the size and field offsets a C compiler gives."""
+    import ctypes as C
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "ripvec_b200.h"\n'
+                   'int main(void){printf("%zu %zu %zu", sizeof(rv_model_desc),'
+                   ' offsetof(rv_model_desc, norm_eps), offsetof(rv_model_desc, max_batch_tokens));return 0;}\n')
+    exe = tmp_path / "layout"
+    subprocess.run([cc, f"-I{HEADER.parent}", str(src), "-o", str(exe)], check=True)
+    size, eps_off, mbt_off = map(int, subprocess.run([str(exe)], capture_output=True, text=True).stdout.split())
+    assert C.sizeof(_lib.ModelDesc) == size
+    assert _lib.ModelDesc.norm_eps.offset == eps_off
+    assert _lib.ModelDesc.max_batch_tokens.offset == mbt_off

@@ -1,0 +1,178 @@
+"""Encoder parity on the GPU through the C ABI (rv_embed_varlen / rv_embed_varlen_device):
+ModernBERT and ClassicBert embeddings against the CPU oracle and the golden fixtures, per-row
+cosine >= 0.999 (bf16) / 0.9999 (fp16), plus the boundary's contract (empty batch, errors,
+batch independence, token-budget packing, device-buffer entry point, safetensors loading)."""
+
+import json
+import struct
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from helpers import TINY_CLASSIC, TINY_MODERN, classic_cfg, modern_cfg, row_cosines
+from oracle import classic_bert, modern_bert
+from ripvec_b200 import MODERNBERT_BASE, BERT_SMALL, EmbedBackend, Encoding, synth
+from ripvec_b200._lib import RvError
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+COS_BF16 = 0.999   # north-star tolerance for bf16
+COS_F16 = 0.9999   # north-star tolerance for fp16
+
+
+@pytest.fixture(scope="module")
+def tiny_modern(cuda_device):
+    g = np.load(GOLDEN / "modernbert_tiny.npz")
+    w = synth.random_weights(TINY_MODERN, seed=int(g["weight_seed"]), qk_std=float(g["qk_std"]))
+    return g, w
+
+
+@pytest.mark.parametrize("dtype,bar", [("bf16", COS_BF16), ("f16", COS_F16)])
+def test_tiny_modernbert_matches_golden(tiny_modern, dtype, bar):
+    g, w = tiny_modern
+    be = EmbedBackend(TINY_MODERN, w, dtype=dtype)
+    out = be.embed_packed(g["ids"], g["cu"])
+    cos = row_cosines(out, g["emb"])
+    assert cos.min() >= bar, cos
+    np.testing.assert_allclose(np.linalg.norm(out, axis=1), 1.0, atol=1e-4)
+    be.close()
+
+
+@pytest.fixture(scope="module")
+def base_weights(cuda_device):
+    return synth.random_weights(MODERNBERT_BASE, seed=1)
+
+
+@pytest.mark.parametrize("dtype,bar,stress", [("bf16", COS_BF16, False), ("bf16", COS_BF16, True),
+                                              ("f16", COS_F16, False)])
+def test_modernbert_base_matches_oracle(base_weights, dtype, bar, stress):
+    w = synth.random_weights(MODERNBERT_BASE, seed=2, qk_std=0.2) if stress else base_weights
+    lengths = np.array([64, 130, 257, 512, 1, 333], np.int32)
+    ids, cu = synth.packed_ids(lengths, MODERNBERT_BASE.vocab, seed=3)
+    be = EmbedBackend(MODERNBERT_BASE, w, dtype=dtype)
+    out = be.embed_packed(ids, cu)
+    ref = modern_bert.embed_batch(w, modern_cfg(MODERNBERT_BASE), ids, cu)
+    cos = row_cosines(out, ref)
+    assert cos.min() >= bar, cos
+    be.close()
+
+
+def test_modernbert_long_sequence_global_and_window(base_weights):
+    """A 2048-token chunk: global layers see every key, local layers only |i-j| <= 64."""
+    lengths = np.array([2048, 700], np.int32)
+    ids, cu = synth.packed_ids(lengths, MODERNBERT_BASE.vocab, seed=4)
+    be = EmbedBackend(MODERNBERT_BASE, base_weights, dtype="f16")
+    out = be.embed_packed(ids, cu)
+    ref = modern_bert.embed_batch(base_weights, modern_cfg(MODERNBERT_BASE), ids, cu)
+    assert row_cosines(out, ref).min() >= COS_F16
+    be.close()
+
+
+def test_boundary_contract(tiny_modern):
+    g, w = tiny_modern
+    be = EmbedBackend(TINY_MODERN, w)
+    assert be.embed_batch([]) == []                       # backend/cpu.rs:909
+    assert be.is_gpu() and not be.supports_clone()
+    assert be.max_tokens() == TINY_MODERN.max_position
+    with pytest.raises(RuntimeError):
+        be.clone_backend()
+    with pytest.raises(RvError):                         # errors propagate, never defaults
+        be.embed_packed(np.array([5, TINY_MODERN.vocab], np.int32), np.array([0, 2], np.int32))
+    with pytest.raises(RvError):
+        n = TINY_MODERN.max_position + 1
+        be.embed_packed(np.zeros(n, np.int32), np.array([0, n], np.int32))
+    # Encoding API, zero-length sequence, order preserved
+    encs = [Encoding(list(g["ids"][g["cu"][i]:g["cu"][i + 1]])) for i in range(len(g["cu"]) - 1)]
+    vecs = np.asarray(be.embed_batch(encs + [Encoding([])]), np.float32)
+    assert vecs.shape == (len(encs) + 1, TINY_MODERN.hidden)
+    assert row_cosines(vecs[:-1], g["emb"]).min() >= COS_BF16
+    assert np.all(vecs[-1] == 0)
+    # batch independence: each chunk alone equals the chunk inside the batch
+    full = be.embed_packed(g["ids"], g["cu"])
+    for i in (0, 3, 7):
+        a, b = int(g["cu"][i]), int(g["cu"][i + 1])
+        alone = be.embed_packed(g["ids"][a:b], np.array([0, b - a], np.int32))
+        np.testing.assert_allclose(alone[0], full[i], atol=1e-6)
+    be.close()
+
+
+def test_token_budget_packing_gives_the_same_result(tiny_modern):
+    g, w = tiny_modern
+    big = EmbedBackend(TINY_MODERN, w, max_batch_tokens=1 << 16)
+    small = EmbedBackend(TINY_MODERN, w, max_batch_tokens=TINY_MODERN.max_position)  # forces many forwards
+    lengths = synth.uniform_lengths(300, 1, 400, seed=5)
+    ids, cu = synth.packed_ids(lengths, TINY_MODERN.vocab, seed=6)
+    a = big.embed_packed(ids, cu)
+    b = small.embed_packed(ids, cu)
+    np.testing.assert_allclose(a, b, atol=1e-6)
+    big.close()
+    small.close()
+
+
+def test_device_entry_point_matches_host_entry_point(tiny_modern):
+    import torch
+
+    g, w = tiny_modern
+    be = EmbedBackend(TINY_MODERN, w)
+    host = be.embed_packed(g["ids"], g["cu"])
+    ids_dev = torch.from_numpy(g["ids"].astype(np.int32)).cuda()
+    out = torch.empty(len(g["cu"]) - 1, TINY_MODERN.hidden, device="cuda", dtype=torch.float32)
+    be.embed_device(ids_dev, g["cu"], out, stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), host)
+    be.close()
+
+
+@pytest.mark.parametrize("pooling", ["cls", "mean"])
+def test_tiny_classicbert_matches_golden(cuda_device, pooling):
+    g = np.load(GOLDEN / "classicbert_tiny.npz")
+    w = synth.random_weights(TINY_CLASSIC, seed=int(g["weight_seed"]), qk_std=float(g["qk_std"]))
+    be = EmbedBackend(TINY_CLASSIC, w, pooling=pooling)
+    out = be.embed_packed(g["ids"], g["cu"])
+    assert row_cosines(out, g["emb_" + pooling]).min() >= COS_BF16
+    be.close()
+
+
+def test_bert_small_matches_oracle(cuda_device):
+    """BASELINE config 1 model (BERT-small, post-LN, learned positions, biases), mean pooling."""
+    w = synth.random_weights(BERT_SMALL, seed=9)
+    lengths = synth.uniform_lengths(6, 32, 256, seed=10)
+    ids, cu = synth.packed_ids(lengths, BERT_SMALL.vocab, seed=11)
+    be = EmbedBackend(BERT_SMALL, w, pooling="mean")
+    out = be.embed_packed(ids, cu)
+    ref = classic_bert.embed_batch(w, classic_cfg(BERT_SMALL), ids, cu, "mean")
+    assert row_cosines(out, ref).min() >= COS_BF16
+    be.close()
+
+
+def _write_safetensors(path: Path, tensors: dict, dtype: str = "F32"):
+    header, blobs, off = {}, [], 0
+    for name, arr in tensors.items():
+        if dtype == "F32":
+            b = np.ascontiguousarray(arr, np.float32).tobytes()
+        else:  # BF16: upper 16 bits, truncation is exact for values that are bf16 already
+            b = (np.ascontiguousarray(arr, np.float32).view(np.uint32) >> 16).astype(np.uint16).tobytes()
+        header[name] = {"dtype": dtype, "shape": list(arr.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    header["__metadata__"] = {"format": "pt"}
+    h = json.dumps(header).encode()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+
+
+@pytest.mark.parametrize("dtype", ["F32", "BF16"])
+def test_safetensors_loading_matches_direct_upload(tiny_modern, tmp_path, dtype):
+    from oracle.ops import to_bf16
+
+    g, w = tiny_modern
+    w = {k: to_bf16(v) for k, v in w.items()}  # exactly representable in both encodings
+    p = tmp_path / "model.safetensors"
+    _write_safetensors(p, {"model." + k: v for k, v in w.items()}, dtype)
+    a = EmbedBackend(TINY_MODERN, None, safetensors=str(p)).embed_packed(g["ids"], g["cu"])
+    b = EmbedBackend(TINY_MODERN, w).embed_packed(g["ids"], g["cu"])
+    np.testing.assert_array_equal(a, b)
