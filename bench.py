@@ -166,23 +166,11 @@ def encoder_workload(args, rank):
 
 
 def sweep_shard(rank, world, n_chunks):
-    """1M log-normal chunks (median 180, sigma 0.8, clip [16,1024]) sharded by token count: sorted
-    by length descending, each chunk to the GPU with the fewest tokens so far."""
-    import heapq
-
-    from ripvec_b200 import synth
+    """1M log-normal chunks (median 180, sigma 0.8, clip [16,1024]) sharded by token count."""
+    from ripvec_b200 import shard, synth
 
     lengths = synth.lognormal_lengths(n_chunks, 180.0, 0.8, 16, 1024, seed=4242)
-    order = np.argsort(-lengths, kind="stable")
-    heap = [(0, g) for g in range(world)]
-    mine = []
-    for i in order:
-        load, g = heapq.heappop(heap)
-        if g == rank:
-            mine.append(i)
-        heapq.heappush(heap, (load + int(lengths[i]), g))
-    mine = np.asarray(sorted(mine), np.int64)
-    return lengths, mine
+    return lengths, shard.shard_by_tokens(lengths, world)[rank]
 
 
 # ------------------------------------------------------------------ reference arm (CPU port)
@@ -463,7 +451,9 @@ def run_scan(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     n_rows, dim, nq, k = 10_000_000, 768, 1024, 100
-    lo, hi = rank * n_rows // world, (rank + 1) * n_rows // world
+    from ripvec_b200 import shard as shard_mod
+
+    lo, hi = shard_mod.row_ranges(n_rows, world)[rank]
     # shard rows generated on the device in blocks (normalised Gaussian, rounded to bf16 by the index)
     gen = torch.Generator(device="cuda").manual_seed(100 + rank)
     shard = torch.empty(hi - lo, dim, device="cuda", dtype=torch.bfloat16)
