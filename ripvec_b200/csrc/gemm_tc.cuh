@@ -34,15 +34,25 @@ struct GemmCfg {
 };
 
 // ---------------------------------------------------------------- epilogues
-// Each epilogue is called for one output row and one group of 64 consecutive accumulator
-// columns [col, col+64): v0 holds columns col..col+31 and v1 holds col+32..col+63, in f32.
+// An epilogue handles one output row and one group of 64 consecutive accumulator columns
+// [col, col+64): v0 holds columns col..col+31 and v1 holds col+32..col+63, in f32.  Global
+// inputs an epilogue needs (residual, rotary tables) are fetched by load() into a Pre object one
+// group ahead of apply(), and for the first group before the accumulator is ready, so their
+// memory latency overlaps the tensor-core work instead of serialising the epilogue.
+
+struct NoPre {};
+struct NoTile {};
 
 template <typename T>
 struct EpiStore {
   T* c;
   int ldc;
-  __device__ __forceinline__ void operator()(int row, int col, const float (&v0)[32],
-                                             const float (&v1)[32]) const {
+  using Pre = NoPre;
+  using Tile = NoTile;
+  __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
+  __device__ __forceinline__ void load(Pre&, int, int) const {}
+  __device__ __forceinline__ void apply(const Pre&, const Tile&, int row, int col, const float (&v0)[32],
+                                        const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
 #pragma unroll
     for (int i = 0; i < 4; ++i) dst[i] = pack8<T>(&v0[8 * i]);
@@ -54,8 +64,12 @@ struct EpiStore {
 struct EpiStoreF32 {
   float* c;
   int ldc;
-  __device__ __forceinline__ void operator()(int row, int col, const float (&v0)[32],
-                                             const float (&v1)[32]) const {
+  using Pre = NoPre;
+  using Tile = NoTile;
+  __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
+  __device__ __forceinline__ void load(Pre&, int, int) const {}
+  __device__ __forceinline__ void apply(const Pre&, const Tile&, int row, int col, const float (&v0)[32],
+                                        const float (&v1)[32]) const {
     float4* dst = reinterpret_cast<float4*>(c + static_cast<size_t>(row) * ldc + col);
 #pragma unroll
     for (int i = 0; i < 8; ++i) dst[i] = make_float4(v0[4 * i], v0[4 * i + 1], v0[4 * i + 2], v0[4 * i + 3]);
@@ -71,18 +85,27 @@ struct EpiResidual {
   T* c;              // read (residual) and written (sum), same element
   int ldc;
   const float* bias; // optional [N]
-  __device__ __forceinline__ void operator()(int row, int col, const float (&v0)[32],
-                                             const float (&v1)[32]) const {
-    uint4* p = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
+  struct Pre {
+    uint4 r[8];
+  };
+  using Tile = NoTile;
+  __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
+  __device__ __forceinline__ void load(Pre& p, int row, int col) const {
+    const uint4* src = reinterpret_cast<const uint4*>(c + static_cast<size_t>(row) * ldc + col);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p.r[i] = src[i];
+  }
+  __device__ __forceinline__ void apply(const Pre& p, const Tile&, int row, int col,
+                                        const float (&v0)[32], const float (&v1)[32]) const {
+    uint4* dst = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
     float r[8], o[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      uint4 u = p[i];
-      unpack8<T>(u, r);
+      unpack8<T>(p.r[i], r);
       const float* v = (i < 4) ? &v0[8 * i] : &v1[8 * (i - 4)];
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = v[j] + (bias ? bias[col + 8 * i + j] : 0.0f) + r[j];
-      p[i] = pack8<T>(o);
+      dst[i] = pack8<T>(o);
     }
   }
 };
@@ -94,8 +117,12 @@ template <typename T>
 struct EpiGeglu {
   T* out;
   int ldo;
-  __device__ __forceinline__ void operator()(int row, int col, const float (&v0)[32],
-                                             const float (&v1)[32]) const {
+  using Pre = NoPre;
+  using Tile = NoTile;
+  __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
+  __device__ __forceinline__ void load(Pre&, int, int) const {}
+  __device__ __forceinline__ void apply(const Pre&, const Tile&, int row, int col, const float (&v0)[32],
+                                        const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * ldo + (col >> 1));
     float o[8];
 #pragma unroll
@@ -113,8 +140,12 @@ struct EpiBiasGelu {
   T* c;
   int ldc;
   const float* bias;
-  __device__ __forceinline__ void operator()(int row, int col, const float (&v0)[32],
-                                             const float (&v1)[32]) const {
+  using Pre = NoPre;
+  using Tile = NoTile;
+  __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
+  __device__ __forceinline__ void load(Pre&, int, int) const {}
+  __device__ __forceinline__ void apply(const Pre&, const Tile&, int row, int col, const float (&v0)[32],
+                                        const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
     float o[8];
 #pragma unroll
@@ -133,8 +164,12 @@ struct EpiBias {
   T* c;
   int ldc;
   const float* bias;
-  __device__ __forceinline__ void operator()(int row, int col, const float (&v0)[32],
-                                             const float (&v1)[32]) const {
+  using Pre = NoPre;
+  using Tile = NoTile;
+  __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
+  __device__ __forceinline__ void load(Pre&, int, int) const {}
+  __device__ __forceinline__ void apply(const Pre&, const Tile&, int row, int col, const float (&v0)[32],
+                                        const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
     float o[8];
 #pragma unroll
@@ -151,7 +186,9 @@ struct EpiBias {
 // < rope_cols) in f32 before rounding; head_dim is 64, so one 64-column group is one head and
 // the rotate-half pairs are (v0[d], v1[d]).  pos[row] is the token's position inside its
 // sequence; cos/sin tables are [max_pos, 32] f32 built on the host like the reference
-// (driver/cpu.rs:670-688 table, :1155-1186 rotation).
+// (driver/cpu.rs:670-688 table, :1155-1186 rotation).  Every head of a row uses the same
+// position, so the row's 32 cos and 32 sin values are fetched once per tile, before the
+// accumulator is ready.
 template <typename T>
 struct EpiQkvRope {
   T* c;
@@ -160,20 +197,33 @@ struct EpiQkvRope {
   const int* pos;
   const float* cos_t;
   const float* sin_t;
-  __device__ __forceinline__ void operator()(int row, int col, const float (&v0)[32],
-                                             const float (&v1)[32]) const {
+  using Pre = NoPre;
+  struct Tile {
+    float4 cv[8], sv[8];
+  };
+  __device__ __forceinline__ void tile_load(Tile& t, int row, int n0) const {
+    if (n0 >= rope_cols) return;
+    const int p = pos[row];
+    const float4* cs = reinterpret_cast<const float4*>(cos_t + static_cast<size_t>(p) * 32);
+    const float4* sn = reinterpret_cast<const float4*>(sin_t + static_cast<size_t>(p) * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      t.cv[i] = cs[i];
+      t.sv[i] = sn[i];
+    }
+  }
+  __device__ __forceinline__ void load(Pre&, int, int) const {}
+  __device__ __forceinline__ void apply(const Pre&, const Tile& t, int row, int col,
+                                        const float (&v0)[32], const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
     if (col < rope_cols) {
-      const int p = pos[row];
-      const float4* cs = reinterpret_cast<const float4*>(cos_t + static_cast<size_t>(p) * 32);
-      const float4* sn = reinterpret_cast<const float4*>(sin_t + static_cast<size_t>(p) * 32);
       float a[8], b[8];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float4 c0 = cs[2 * i], c1 = cs[2 * i + 1];
-        float4 s0 = sn[2 * i], s1 = sn[2 * i + 1];
-        float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-        float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const float cc[8] = {t.cv[2 * i].x, t.cv[2 * i].y, t.cv[2 * i].z, t.cv[2 * i].w,
+                             t.cv[2 * i + 1].x, t.cv[2 * i + 1].y, t.cv[2 * i + 1].z, t.cv[2 * i + 1].w};
+        const float ss[8] = {t.sv[2 * i].x, t.sv[2 * i].y, t.sv[2 * i].z, t.sv[2 * i].w,
+                             t.sv[2 * i + 1].x, t.sv[2 * i + 1].y, t.sv[2 * i + 1].z, t.sv[2 * i + 1].w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float f = v0[8 * i + j], s = v1[8 * i + j];
@@ -319,20 +369,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) { ok = false; break; }
-      tc_fence_after();
       const int m0 = (t / num_n) * kGemmBM;
       const int n0 = (t % num_n) * BN;
       const int row = m0 + quad * 32 + lane;
+      const bool live = row < M;
+      typename Epi::Pre pre[2];
+      typename Epi::Tile tile;
+      if (live) {  // before the accumulator is ready
+        epi.tile_load(tile, row, n0);
+        epi.load(pre[0], row, n0);
+      }
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) { ok = false; break; }
+      tc_fence_after();
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
+#pragma unroll
       for (int g = 0; g < BN / 64; ++g) {
+        if (g + 1 < BN / 64 && live) epi.load(pre[(g + 1) & 1], row, n0 + (g + 1) * 64);
         float v0[32], v1[32];
         tmem_ld32(tbase + g * 64, v0);
         tmem_ld32(tbase + g * 64 + 32, v1);
         tc_wait_ld();
-        if (row < M) epi(row, n0 + g * 64, v0, v1);
+        if (live) epi.apply(pre[g & 1], tile, row, n0 + g * 64, v0, v1);
       }
       tc_fence_before();
       __syncwarp();
