@@ -147,6 +147,22 @@ int rv_topk_merge_device(int device, const int64_t* idx_in, const double* score_
                          int32_t n_lists, int32_t nq, int32_t k, float threshold,
                          int64_t* idx_out, float* score_out, double* score64_out, void* stream);
 
+/* The same exact top-k as rv_index_topk_device for callers that cannot allocate device memory
+ * (a host whose allocator or memory pool owns the whole device budget, or a serving thread that
+ * must not let cudaMalloc / cudaFree synchronise the device).  No counterpart in the reference:
+ * it exists only for such callers.  All scratch lives in one fixed device array inside the
+ * library (about 4.2 MiB, held by every GPU that loads the library until exit); the call makes
+ * no cudaMalloc / cudaFree.  Limits: nq <= 16 queries, k <= 64, rows of at most 4096
+ * dimensions; larger requests return RV_E_INVALID.  Device buffers as in rv_index_topk_device;
+ * runs on `stream` (0 = the index's stream) and returns when the results are written.  The first
+ * call on a device looks up the array's device address; make it before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race and must be serialised by the
+ * caller.  Near-tied scores that need a wider candidate list than the array holds return
+ * RV_E_DEVICE (rv_index_topk_device handles them). */
+int rv_index_topk_noalloc(rv_index* idx, const float* queries_dev, int32_t nq, int32_t k,
+                          float threshold, int64_t* out_idx_dev, float* out_score_dev,
+                          double* out_score64_dev, void* stream);
+
 /* ---------------------------------------------------------------- single-kernel entry points
  * Used by the parity tests to check one kernel against the CPU oracle.  Device pointers. */
 /* C[M,N] (f32 or act) = A[M,K] B[N,K]^T with A, B of act dtype (RV_DTYPE_BF16/F16). */

@@ -86,6 +86,7 @@ SIGNATURES = {
     "rv_index_set_base": (C.c_int, [vp, i64]),
     "rv_index_topk": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_index_topk_device": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
+    "rv_index_topk_noalloc": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_topk_merge_device": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, f32, vp, vp, vp, vp]),
     "rv_op_gemm": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "rv_op_attention": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, f32, vp]),

@@ -11,51 +11,10 @@
 
 #include "../../include/ripvec_b200.h"
 #include "engine.h"
+#include "index_impl.h"
 #include "kernels.h"
 #include "scan.h"
 #include "tmap.h"
-
-template <typename T>
-struct DevBuf {
-  T* p = nullptr;
-  size_t cap = 0;
-  // Ensures room for `need` elements (contents are not preserved).  False on allocation failure.
-  bool reserve(size_t need) {
-    if (p && cap >= need) return true;
-    if (p) cudaFree(p);
-    p = nullptr;
-    cap = 0;
-    if (cudaMalloc(reinterpret_cast<void**>(&p), (need ? need : 1) * sizeof(T)) != cudaSuccess) return false;
-    cap = need;
-    return true;
-  }
-  void release() {
-    if (p) cudaFree(p);
-    p = nullptr;
-    cap = 0;
-  }
-};
-
-struct rv_index {
-  int device = 0;
-  std::mutex mu;
-  std::string err;
-  cudaStream_t stream = nullptr;
-  __nv_bfloat16* db = nullptr;
-  int64_t n = 0;
-  int dim = 0;
-  int64_t base = 0;
-  double max_norm = 0.0;
-  CUtensorMap tmap_db;
-  unsigned int* d_err = nullptr;
-  // scratch, grown on demand
-  DevBuf<float> scores, qf, list_s, os;
-  DevBuf<__nv_bfloat16> qb;
-  DevBuf<int64_t> list_i, oi;
-  DevBuf<int> list_n, cnt, guard;
-  DevBuf<double> os64;
-  int64_t launches = 0;
-};
 
 namespace {
 
