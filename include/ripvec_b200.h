@@ -165,7 +165,8 @@ int rv_index_topk_noalloc(rv_index* idx, const float* queries_dev, int32_t nq, i
 
 /* ---------------------------------------------------------------- single-kernel entry points
  * Used by the parity tests to check one kernel against the CPU oracle.  Device pointers. */
-/* C[M,N] (f32 or act) = A[M,K] B[N,K]^T with A, B of act dtype (RV_DTYPE_BF16/F16). */
+/* C[M,N] (f32 or act) = A[M,K] B[N,K]^T with A, B of act dtype (RV_DTYPE_BF16/F16); bn = 128 or
+ * 256 (one-CTA 128 x bn tiles) or 512 (two-CTA 256 x 256 tiles). */
 int rv_op_gemm(int32_t act_dtype, const void* a, const void* b, void* c, int32_t c_dtype,
                int32_t M, int32_t N, int32_t K, int32_t bn, void* stream);
 /* Attention over packed qkv [T, 3*heads*head_dim]; window_half < 0 = global. */

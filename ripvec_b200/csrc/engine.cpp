@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <memory>
@@ -238,7 +239,9 @@ int up_matrix(rv_ctx* c, const std::vector<float>& v, int rows, int cols, int bn
   m->cols = cols;
   m->bn = bn;
   if (!rv::make_tmap_2d_16bit(&m->tmap, m->ptr, c->adt == Act::kBf16, cols, rows,
-                              uint64_t(cols) * 2, 64, bn, &why))
+                              uint64_t(cols) * 2, 64, bn, &why) ||
+      !rv::make_tmap_2d_16bit(&m->tmap_half, m->ptr, c->adt == Act::kBf16, cols, rows,
+                              uint64_t(cols) * 2, 64, 128, &why))
     return fail(c, RV_E_CUDA, why);
   return RV_OK;
 }
@@ -259,6 +262,34 @@ void build_rope(int max_pos, int head_dim, float theta, std::vector<float>* cs,
     }
 }
 
+// Folds a LayerNorm gain into the following projection: W'[n,k] = W[n,k] * gamma[k] (f32, then the
+// upload rounds to the device dtype).  Returns c_n = sum_k W'[n,k] over the rounded values, the
+// column sums the LayerNorm-folding epilogues subtract (mu * c_n).
+std::vector<float> fold_gamma(std::vector<float>* w, int rows, int cols, const std::vector<float>& gamma,
+                              Act adt) {
+  std::vector<float> cs(rows);
+  for (int r = 0; r < rows; ++r) {
+    double sum = 0.0;
+    float* row = w->data() + size_t(r) * cols;
+    for (int k = 0; k < cols; ++k) {
+      row[k] *= gamma[k];
+      float q;
+      if (adt == Act::kBf16) {
+        const uint32_t b = uint32_t(rv::f32_to_bf16_bits(row[k])) << 16;
+        std::memcpy(&q, &b, 4);
+      } else {
+        const uint16_t h = rv::f32_to_f16_bits(row[k]);
+        __half hv;
+        std::memcpy(&hv, &h, 2);
+        q = __half2float(hv);
+      }
+      sum += q;
+    }
+    cs[r] = static_cast<float>(sum);
+  }
+  return cs;
+}
+
 int finalize_modern(rv_ctx* c) {
   const int H = c->d.hidden, I = c->d.intermediate, L = c->d.num_layers;
   const std::vector<float>* w;
@@ -274,8 +305,24 @@ int finalize_modern(rv_ctx* c) {
     const std::string p = "layers." + std::to_string(i) + ".";
     rv::LayerWeights& lw = c->layers[i];
     lw.is_global = (i % c->d.global_every_n) == 0;
+    const std::vector<float>* attn_g = nullptr;
+    const std::vector<float>* mlp_g = nullptr;
+    if (i > 0) {
+      if ((rc = need(c, p + "attn_norm.weight", &attn_g))) return rc;
+      if ((rc = up_f32(c, *attn_g, &lw.attn_norm))) return rc;
+    }
+    if ((rc = need(c, p + "mlp_norm.weight", &mlp_g))) return rc;
+    if ((rc = up_f32(c, *mlp_g, &lw.mlp_norm))) return rc;
+
     if ((rc = need(c, p + "attn.Wqkv.weight", &w))) return rc;
-    if ((rc = up_matrix(c, *w, 3 * H, H, 256, &lw.wqkv))) return rc;
+    if (c->ln_fused && attn_g) {
+      std::vector<float> wq(*w);
+      std::vector<float> cs = fold_gamma(&wq, 3 * H, H, *attn_g, c->adt);
+      if ((rc = up_matrix(c, wq, 3 * H, H, 256, &lw.wqkv))) return rc;
+      if ((rc = up_f32(c, cs, &lw.csum_qkv))) return rc;
+    } else if ((rc = up_matrix(c, *w, 3 * H, H, 256, &lw.wqkv))) {
+      return rc;
+    }
     if ((rc = need(c, p + "attn.Wo.weight", &w))) return rc;
     if ((rc = up_matrix(c, *w, H, H, 256, &lw.wo))) return rc;
     if ((rc = need(c, p + "mlp.Wi.weight", &w))) return rc;
@@ -287,15 +334,13 @@ int finalize_modern(rv_ctx* c) {
       const int src = within < 32 ? g * 32 + within : I + g * 32 + (within - 32);
       std::memcpy(&wi[size_t(r) * H], &(*w)[size_t(src) * H], sizeof(float) * H);
     }
+    if (c->ln_fused) {
+      std::vector<float> cs = fold_gamma(&wi, 2 * I, H, *mlp_g, c->adt);
+      if ((rc = up_f32(c, cs, &lw.csum_wi))) return rc;
+    }
     if ((rc = up_matrix(c, wi, 2 * I, H, 256, &lw.wi))) return rc;
     if ((rc = need(c, p + "mlp.Wo.weight", &w))) return rc;
     if ((rc = up_matrix(c, *w, H, I, 256, &lw.wo2))) return rc;
-    if (i > 0) {
-      if ((rc = need(c, p + "attn_norm.weight", &w))) return rc;
-      if ((rc = up_f32(c, *w, &lw.attn_norm))) return rc;
-    }
-    if ((rc = need(c, p + "mlp_norm.weight", &w))) return rc;
-    if ((rc = up_f32(c, *w, &lw.mlp_norm))) return rc;
   }
   const int hd = H / c->d.num_heads;
   for (int g = 0; g < 2; ++g) {
@@ -384,6 +429,11 @@ int alloc_workspaces(rv_ctx* c) {
   c->qkv = dalloc(c, size_t(T) * 3 * H * es);
   c->cbuf = dalloc(c, size_t(T) * H * es);
   c->act = dalloc(c, size_t(T) * I * es);
+  if (is_modern(c) && c->ln_fused) {
+    c->stats_a = dalloc(c, size_t(T) * 4 * sizeof(float2));
+    c->stats_b = dalloc(c, size_t(T) * 4 * sizeof(float2));
+    if (!c->stats_a || !c->stats_b) return fail(c, RV_E_NOMEM, "workspace allocation failed");
+  }
   c->ids_d = static_cast<int*>(dalloc(c, size_t(T) * 4));
   c->pos_d = static_cast<int*>(dalloc(c, size_t(T) * 4));
   c->meta_d = static_cast<int*>(dalloc(c, size_t(2) * (c->n_max + 1) * 4));
@@ -408,10 +458,11 @@ int alloc_workspaces(rv_ctx* c) {
 
 int gemm(rv_ctx* c, const CUtensorMap& A, const rv::DeviceMatrix& B, int M, GemmEpi epi, void* out,
          int ldc, const float* bias = nullptr, int rope_cols = 0, const float* cs = nullptr,
-         const float* sn = nullptr) {
+         const float* sn = nullptr, void* stats = nullptr, const float* csum = nullptr) {
   GemmArgs a{};
   a.tmA = &A;
-  a.tmB = &B.tmap;
+  a.pair = c->gemm_pair && B.bn == 256 && B.rows % 256 == 0;
+  a.tmB = a.pair ? &B.tmap_half : &B.tmap;
   a.M = M;
   a.N = B.rows;
   a.K = B.cols;
@@ -424,6 +475,11 @@ int gemm(rv_ctx* c, const CUtensorMap& A, const rv::DeviceMatrix& B, int M, Gemm
   a.pos = c->pos_d;
   a.cos_t = cs;
   a.sin_t = sn;
+  a.stats = stats;
+  a.stats_ld = 4;
+  a.stats_n = c->d.hidden / 256;
+  a.csum = csum;
+  a.eps = c->d.norm_eps;
   RV_LAUNCH_K(c, RV_KIND_GEMM, 2.0 * double(M) * a.N * a.K, rv::gemm_tc(c->adt, a, c->d_err, c->stream));
   return RV_OK;
 }
@@ -444,19 +500,46 @@ int forward(rv_ctx* c, const int* ids, int T, int n, int total_q_tiles, double p
     for (int l = 0; l < c->d.num_layers; ++l) {
       const rv::LayerWeights& lw = c->layers[l];
       const int g = lw.is_global ? 0 : 1;
+      const int wh = lw.is_global ? -1 : c->d.local_window / 2;
       int rc;
+      if (c->ln_fused) {
+        // LayerNorms folded into the projections: QKV / Wi read the raw residual rows and the
+        // row statistics the previous residual epilogue wrote (stats_b after the MLP block,
+        // stats_a after the attention block); layer 0 has no attention LayerNorm.
+        if (l == 0) {
+          if ((rc = gemm(c, c->map_x, lw.wqkv, T, GemmEpi::kQkvRope, c->qkv, 3 * H, nullptr, 2 * H,
+                         c->rope_cos[g], c->rope_sin[g])))
+            return rc;
+        } else if ((rc = gemm(c, c->map_x, lw.wqkv, T, GemmEpi::kNormQkvRope, c->qkv, 3 * H, nullptr, 2 * H,
+                              c->rope_cos[g], c->rope_sin[g], c->stats_b, lw.csum_qkv))) {
+          return rc;
+        }
+        RV_LAUNCH_K(c, RV_KIND_ATTENTION, 4.0 * H * (lw.is_global ? pairs_global : pairs_local),
+                    rv::attention_varlen(c->adt, c->qkv, c->cbuf, cu, qts, n, total_q_tiles, heads, hd, wh,
+                                         scale, st));
+        if ((rc = gemm(c, c->map_c, lw.wo, T, GemmEpi::kResidualStats, c->x, H, nullptr, 0, nullptr, nullptr,
+                       c->stats_a)))
+          return rc;
+        if ((rc = gemm(c, c->map_x, lw.wi, T, GemmEpi::kNormGeglu, c->act, c->d.intermediate, nullptr, 0, nullptr,
+                       nullptr, c->stats_a, lw.csum_wi)))
+          return rc;
+        if ((rc = gemm(c, c->map_act, lw.wo2, T, GemmEpi::kResidualStats, c->x, H, nullptr, 0, nullptr, nullptr,
+                       c->stats_b)))
+          return rc;
+        continue;
+      }
       if (l > 0)
         RV_LAUNCH_K(c, RV_KIND_NORM, 0, rv::layernorm(c->adt, c->x, c->hn, T, H, lw.attn_norm, nullptr,
-                                   c->d.norm_eps, st));
+                                                      c->d.norm_eps, st));
       if ((rc = gemm(c, l == 0 ? c->map_x : c->map_hn, lw.wqkv, T, GemmEpi::kQkvRope, c->qkv,
                      3 * H, nullptr, 2 * H, c->rope_cos[g], c->rope_sin[g])))
         return rc;
       RV_LAUNCH_K(c, RV_KIND_ATTENTION, 4.0 * H * (lw.is_global ? pairs_global : pairs_local),
-                  rv::attention_varlen(c->adt, c->qkv, c->cbuf, cu, qts, n, total_q_tiles, heads, hd,
-                                       lw.is_global ? -1 : c->d.local_window / 2, scale, st));
+                  rv::attention_varlen(c->adt, c->qkv, c->cbuf, cu, qts, n, total_q_tiles, heads, hd, wh,
+                                       scale, st));
       if ((rc = gemm(c, c->map_c, lw.wo, T, GemmEpi::kResidual, c->x, H))) return rc;
-      RV_LAUNCH_K(c, RV_KIND_NORM, 0, rv::layernorm(c->adt, c->x, c->hn, T, H, lw.mlp_norm, nullptr, c->d.norm_eps,
-                                 st));
+      RV_LAUNCH_K(c, RV_KIND_NORM, 0, rv::layernorm(c->adt, c->x, c->hn, T, H, lw.mlp_norm, nullptr,
+                                                    c->d.norm_eps, st));
       if ((rc = gemm(c, c->map_hn, lw.wi, T, GemmEpi::kGeglu, c->act, c->d.intermediate)))
         return rc;
       if ((rc = gemm(c, c->map_act, lw.wo2, T, GemmEpi::kResidual, c->x, H))) return rc;
@@ -597,6 +680,8 @@ int rv_create(const rv_model_desc* desc, int device, rv_ctx** out) {
   c->d = d;
   c->device = device;
   c->adt = d.dtype == RV_DTYPE_BF16 ? Act::kBf16 : Act::kF16;
+  if (const char* e = std::getenv("RV_GEMM_2SM")) c->gemm_pair = std::strcmp(e, "0") != 0;
+  if (const char* e = std::getenv("RV_LN_FUSED")) c->ln_fused = std::strcmp(e, "0") != 0;
   c->t_max = d.max_batch_tokens > 0 ? d.max_batch_tokens : 262144;
   if (c->t_max < d.max_position) c->t_max = d.max_position;
   c->n_max = 65536;

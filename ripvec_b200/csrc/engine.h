@@ -27,6 +27,7 @@ struct DeviceMatrix {
   void* ptr = nullptr;   // [rows, cols] 16-bit, row-major
   int rows = 0, cols = 0;
   CUtensorMap tmap;      // B-operand map, box 64 x bn
+  CUtensorMap tmap_half; // box 64 x 128: each CTA's half of a two-CTA 256-wide tile
   int bn = 256;
 };
 
@@ -34,6 +35,8 @@ struct LayerWeights {
   DeviceMatrix wqkv, wo, wi, wo2;
   float* attn_norm = nullptr;  // ModernBERT (null for layer 0)
   float* mlp_norm = nullptr;
+  float* csum_qkv = nullptr;   // column sums of the LayerNorm-folded Wqkv (layers > 0)
+  float* csum_wi = nullptr;    // column sums of the LayerNorm-folded, interleaved Wi
   float* bqkv = nullptr;       // ClassicBert biases and post-LN parameters
   float* bo = nullptr;
   float* ln1_w = nullptr;
@@ -51,6 +54,8 @@ struct rv_ctx {
   rv_model_desc d{};
   int device = 0;
   rv::Act adt = rv::Act::kBf16;  // device storage dtype
+  bool ln_fused = true;          // ModernBERT LayerNorms folded into the GEMMs (RV_LN_FUSED=0 turns off)
+  bool gemm_pair = true;         // two-CTA GEMM tiles for 256-wide projections (RV_GEMM_2SM=0 turns off)
   std::mutex mu;
   std::string err;
   cudaStream_t stream = nullptr;
@@ -78,6 +83,8 @@ struct rv_ctx {
   void* qkv = nullptr;  // [t_max, 3*hidden]
   void* cbuf = nullptr; // attention context [t_max, hidden]
   void* act = nullptr;  // MLP activation [t_max, intermediate]
+  void* stats_a = nullptr;  // float2 LayerNorm partials [t_max, 4] of x after the attention block
+  void* stats_b = nullptr;  // ... and after the MLP block
   int* ids_d = nullptr;
   int* pos_d = nullptr;
   int* meta_d = nullptr;  // cu_seqlens (n_max+1) then q-tile starts (n_max+1)

@@ -31,6 +31,7 @@ struct GemmCfg {
   static constexpr int kStages = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
   static constexpr uint32_t kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+  static constexpr int kEpiSmemBytes = 10240;  // staged epilogue vectors (<= 2560 floats)
 };
 
 // ---------------------------------------------------------------- epilogues
@@ -49,9 +50,10 @@ struct EpiStore {
   int ldc;
   using Pre = NoPre;
   using Tile = NoTile;
+  __device__ __forceinline__ void stage(float*, int, int) const {}
   __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
   __device__ __forceinline__ void load(Pre&, int, int) const {}
-  __device__ __forceinline__ void apply(const Pre&, const Tile&, int row, int col, const float (&v0)[32],
+  __device__ __forceinline__ void apply(const Pre&, Tile&, int row, int col, const float (&v0)[32],
                                         const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
 #pragma unroll
@@ -66,9 +68,10 @@ struct EpiStoreF32 {
   int ldc;
   using Pre = NoPre;
   using Tile = NoTile;
+  __device__ __forceinline__ void stage(float*, int, int) const {}
   __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
   __device__ __forceinline__ void load(Pre&, int, int) const {}
-  __device__ __forceinline__ void apply(const Pre&, const Tile&, int row, int col, const float (&v0)[32],
+  __device__ __forceinline__ void apply(const Pre&, Tile&, int row, int col, const float (&v0)[32],
                                         const float (&v1)[32]) const {
     float4* dst = reinterpret_cast<float4*>(c + static_cast<size_t>(row) * ldc + col);
 #pragma unroll
@@ -89,13 +92,14 @@ struct EpiResidual {
     uint4 r[8];
   };
   using Tile = NoTile;
+  __device__ __forceinline__ void stage(float*, int, int) const {}
   __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
   __device__ __forceinline__ void load(Pre& p, int row, int col) const {
     const uint4* src = reinterpret_cast<const uint4*>(c + static_cast<size_t>(row) * ldc + col);
 #pragma unroll
     for (int i = 0; i < 8; ++i) p.r[i] = src[i];
   }
-  __device__ __forceinline__ void apply(const Pre& p, const Tile&, int row, int col,
+  __device__ __forceinline__ void apply(const Pre& p, Tile&, int row, int col,
                                         const float (&v0)[32], const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
     float r[8], o[8];
@@ -119,9 +123,10 @@ struct EpiGeglu {
   int ldo;
   using Pre = NoPre;
   using Tile = NoTile;
+  __device__ __forceinline__ void stage(float*, int, int) const {}
   __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
   __device__ __forceinline__ void load(Pre&, int, int) const {}
-  __device__ __forceinline__ void apply(const Pre&, const Tile&, int row, int col, const float (&v0)[32],
+  __device__ __forceinline__ void apply(const Pre&, Tile&, int row, int col, const float (&v0)[32],
                                         const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * ldo + (col >> 1));
     float o[8];
@@ -142,9 +147,10 @@ struct EpiBiasGelu {
   const float* bias;
   using Pre = NoPre;
   using Tile = NoTile;
+  __device__ __forceinline__ void stage(float*, int, int) const {}
   __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
   __device__ __forceinline__ void load(Pre&, int, int) const {}
-  __device__ __forceinline__ void apply(const Pre&, const Tile&, int row, int col, const float (&v0)[32],
+  __device__ __forceinline__ void apply(const Pre&, Tile&, int row, int col, const float (&v0)[32],
                                         const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
     float o[8];
@@ -166,9 +172,10 @@ struct EpiBias {
   const float* bias;
   using Pre = NoPre;
   using Tile = NoTile;
+  __device__ __forceinline__ void stage(float*, int, int) const {}
   __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
   __device__ __forceinline__ void load(Pre&, int, int) const {}
-  __device__ __forceinline__ void apply(const Pre&, const Tile&, int row, int col, const float (&v0)[32],
+  __device__ __forceinline__ void apply(const Pre&, Tile&, int row, int col, const float (&v0)[32],
                                         const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
     float o[8];
@@ -201,6 +208,7 @@ struct EpiQkvRope {
   struct Tile {
     float4 cv[8], sv[8];
   };
+  __device__ __forceinline__ void stage(float*, int, int) const {}
   __device__ __forceinline__ void tile_load(Tile& t, int row, int n0) const {
     if (n0 >= rope_cols) return;
     const int p = pos[row];
@@ -213,7 +221,7 @@ struct EpiQkvRope {
     }
   }
   __device__ __forceinline__ void load(Pre&, int, int) const {}
-  __device__ __forceinline__ void apply(const Pre&, const Tile& t, int row, int col,
+  __device__ __forceinline__ void apply(const Pre&, Tile& t, int row, int col,
                                         const float (&v0)[32], const float (&v1)[32]) const {
     uint4* dst = reinterpret_cast<uint4*>(c + static_cast<size_t>(row) * ldc + col);
     if (col < rope_cols) {
@@ -364,6 +372,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    // Epilogue-constant vectors (column sums of folded weights) go to shared memory once.
+    float* epi_smem = reinterpret_cast<float*>(smem + kStages * Cfg::kStageBytes + 256);
+    epi.stage(epi_smem, threadIdx.x - 64, 128);
+    asm volatile("bar.sync 1, 128;" ::: "memory");
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
@@ -421,14 +433,14 @@ cudaError_t launch_gemm_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, int M
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<T, BN, Epi>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::kSmemBytes);
+                                         Cfg::kSmemBytes + Cfg::kEpiSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
   if (M <= 0) return cudaSuccess;
   const int tiles = ((M + kGemmBM - 1) / kGemmBM) * (N / BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
-  gemm_tc_kernel<T, BN, Epi><<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(
+  gemm_tc_kernel<T, BN, Epi><<<grid, kGemmThreads, Cfg::kSmemBytes + Cfg::kEpiSmemBytes, stream>>>(
       tmA, tmB, M, N, K, b_row_offset, epi, err);
   return cudaGetLastError();
 }

@@ -26,6 +26,9 @@ enum class GemmEpi {
   kBias = 4,       // C = A B^T + bias
   kBiasGelu = 5,   // C = gelu(A B^T + bias)
   kStoreF32 = 6,   // C(f32) = A B^T
+  kResidualStats = 7,  // C += A B^T and per-256-column (mean, M2) LayerNorm partials of C
+  kNormQkvRope = 8,    // LayerNorm folded (A = raw rows + partials), then QKV + rotary
+  kNormGeglu = 9,      // LayerNorm folded, then GeGLU
 };
 
 struct GemmArgs {
@@ -34,6 +37,7 @@ struct GemmArgs {
   int M, N, K;
   int bn;                  // 128 or 256 (N % bn == 0)
   int b_row_offset;        // added to the B-operand row coordinate (chunked scans)
+  bool pair;               // two-CTA 256 x 256 tiles (tmB must then have a 64 x 128 box)
   GemmEpi epi;
   void* c;                 // output (or in/out for kResidual)
   int ldc;                 // elements
@@ -42,6 +46,11 @@ struct GemmArgs {
   const int* pos;          // kQkvRope: [M] position inside the sequence
   const float* cos_t;      // kQkvRope: [max_pos, 32]
   const float* sin_t;
+  void* stats;             // float2 partials: written by kResidualStats, read by kNorm*
+  int stats_ld;            // partials per row in the buffer
+  int stats_n;             // kNorm*: partials that make up one row (hidden / 256)
+  const float* csum;       // kNorm*: column sums of the folded weights, [N]
+  float eps;               // kNorm*: LayerNorm epsilon
 };
 
 cudaError_t gemm_tc(Act act, const GemmArgs& a, unsigned int* err, cudaStream_t st);

@@ -46,13 +46,15 @@ int rv_op_gemm(int32_t act_dtype, const void* a, const void* b, void* c, int32_t
                int32_t M, int32_t N, int32_t K, int32_t bn, void* stream) {
   if (act_dtype != RV_DTYPE_BF16 && act_dtype != RV_DTYPE_F16) return RV_E_INVALID;
   if (c_dtype != RV_DTYPE_F32 && c_dtype != act_dtype) return RV_E_INVALID;
+  const bool pair = bn == 512;  // two-CTA 256 x 256 tiles
+  if (pair) bn = 256;
   if (M <= 0 || N <= 0 || K <= 0 || K % 64 != 0 || (bn != 128 && bn != 256) || N % bn != 0)
     return RV_E_INVALID;
   const bool bf = act_dtype == RV_DTYPE_BF16;
   CUtensorMap ta, tb;
   std::string why;
   if (!rv::make_tmap_2d_16bit(&ta, a, bf, K, M, uint64_t(K) * 2, 64, 128, &why)) return RV_E_INVALID;
-  if (!rv::make_tmap_2d_16bit(&tb, b, bf, K, N, uint64_t(K) * 2, 64, bn, &why)) return RV_E_INVALID;
+  if (!rv::make_tmap_2d_16bit(&tb, b, bf, K, N, uint64_t(K) * 2, 64, pair ? 128 : bn, &why)) return RV_E_INVALID;
   unsigned int* err = op_err_word();
   if (!err) return RV_E_NOMEM;
   rv::GemmArgs g{};
@@ -62,6 +64,7 @@ int rv_op_gemm(int32_t act_dtype, const void* a, const void* b, void* c, int32_t
   g.N = N;
   g.K = K;
   g.bn = bn;
+  g.pair = pair;
   g.epi = c_dtype == RV_DTYPE_F32 ? rv::GemmEpi::kStoreF32 : rv::GemmEpi::kStore;
   g.c = c;
   g.ldc = N;

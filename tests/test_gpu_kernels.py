@@ -22,7 +22,10 @@ def _stream():
 @pytest.mark.parametrize("act", ["bf16", "f16"])
 @pytest.mark.parametrize("M,N,K,bn", [(1, 256, 64, 256), (127, 256, 768, 256), (128, 768, 768, 256),
                                       (1000, 2304, 768, 256), (4096, 768, 1152, 256), (300, 1152, 384, 128),
-                                      (513, 384, 1536, 128), (20000, 768, 768, 256)])
+                                      (513, 384, 1536, 128), (20000, 768, 768, 256),
+                                      # bn=512: two-CTA 256 x 256 tiles (tcgen05.mma.cta_group::2)
+                                      (1, 256, 64, 512), (255, 768, 768, 512), (257, 2304, 768, 512),
+                                      (4096, 768, 1152, 512), (20000, 2304, 768, 512)])
 def test_gemm_matches_fp32(cuda_device, act, M, N, K, bn):
     torch = _torch()
     from ripvec_b200 import _lib as L

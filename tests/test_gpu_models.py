@@ -180,3 +180,20 @@ def test_safetensors_loading_matches_direct_upload(tiny_modern, tmp_path, dtype)
     a = EmbedBackend(TINY_MODERN, None, safetensors=str(p)).embed_packed(g["ids"], g["cu"])
     b = EmbedBackend(TINY_MODERN, w).embed_packed(g["ids"], g["cu"])
     np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.parametrize("env", ["RV_LN_FUSED", "RV_GEMM_2SM"])
+def test_kernel_variants_agree(base_weights, monkeypatch, env):
+    """LayerNorm folded into the GEMMs vs separate LayerNorm kernels, and two-CTA vs one-CTA GEMM
+    tiles: both variants of each pair must give the same embeddings (and match the oracle)."""
+    lengths = np.array([64, 300, 512, 1, 129], np.int32)
+    ids, cu = synth.packed_ids(lengths, MODERNBERT_BASE.vocab, seed=21)
+    outs = []
+    for flag in ("1", "0"):
+        monkeypatch.setenv(env, flag)
+        be = EmbedBackend(MODERNBERT_BASE, base_weights, dtype="bf16")
+        outs.append(be.embed_packed(ids, cu))
+        be.close()
+    assert row_cosines(outs[0], outs[1]).min() >= 0.9999
+    ref = modern_bert.embed_batch(base_weights, modern_cfg(MODERNBERT_BASE), ids, cu)
+    assert row_cosines(outs[0], ref).min() >= COS_BF16
