@@ -451,7 +451,9 @@ int alloc_workspaces(rv_ctx* c) {
   if (!rv::make_tmap_2d_16bit(&c->map_x, c->x, bf, H, T, uint64_t(H) * 2, 64, 128, &why) ||
       !rv::make_tmap_2d_16bit(&c->map_hn, c->hn, bf, H, T, uint64_t(H) * 2, 64, 128, &why) ||
       !rv::make_tmap_2d_16bit(&c->map_c, c->cbuf, bf, H, T, uint64_t(H) * 2, 64, 128, &why) ||
-      !rv::make_tmap_2d_16bit(&c->map_act, c->act, bf, I, T, uint64_t(I) * 2, 64, 128, &why))
+      !rv::make_tmap_2d_16bit(&c->map_act, c->act, bf, I, T, uint64_t(I) * 2, 64, 128, &why) ||
+      !rv::make_tmap_2d_16bit(&c->map_qkv_out, c->qkv, bf, 3 * H, T, uint64_t(3 * H) * 2, 64, 128, &why) ||
+      !rv::make_tmap_2d_16bit(&c->map_act_out, c->act, bf, I, T, uint64_t(I) * 2, 32, 128, &why, 64))
     return fail(c, RV_E_CUDA, why);
   return RV_OK;
 }
@@ -480,6 +482,11 @@ int gemm(rv_ctx* c, const CUtensorMap& A, const rv::DeviceMatrix& B, int M, Gemm
   a.stats_n = c->d.hidden / 256;
   a.csum = csum;
   a.eps = c->d.norm_eps;
+  if (a.pair && c->tma_epi) {
+    if (epi == GemmEpi::kQkvRope || epi == GemmEpi::kNormQkvRope) a.tmC = &c->map_qkv_out;
+    else if (epi == GemmEpi::kResidualStats) a.tmC = &c->map_x;
+    else if (epi == GemmEpi::kNormGeglu) a.tmC = &c->map_act_out;
+  }
   RV_LAUNCH_K(c, RV_KIND_GEMM, 2.0 * double(M) * a.N * a.K, rv::gemm_tc(c->adt, a, c->d_err, c->stream));
   return RV_OK;
 }
@@ -682,6 +689,7 @@ int rv_create(const rv_model_desc* desc, int device, rv_ctx** out) {
   c->adt = d.dtype == RV_DTYPE_BF16 ? Act::kBf16 : Act::kF16;
   if (const char* e = std::getenv("RV_GEMM_2SM")) c->gemm_pair = std::strcmp(e, "0") != 0;
   if (const char* e = std::getenv("RV_LN_FUSED")) c->ln_fused = std::strcmp(e, "0") != 0;
+  if (const char* e = std::getenv("RV_TMA_EPI")) c->tma_epi = std::strcmp(e, "0") != 0;
   c->t_max = d.max_batch_tokens > 0 ? d.max_batch_tokens : 262144;
   if (c->t_max < d.max_position) c->t_max = d.max_position;
   c->n_max = 65536;

@@ -92,6 +92,8 @@ struct rv_ctx {
   int* meta_h = nullptr;  // pinned staging of meta_d
   cudaEvent_t meta_evt = nullptr;
   CUtensorMap map_x, map_hn, map_c, map_act;
+  CUtensorMap map_qkv_out, map_act_out;  // TMA-staged epilogue outputs (x uses map_x)
+  bool tma_epi = true;                   // TMA-staged GEMM epilogues (RV_TMA_EPI=0 turns off)
 
   std::vector<void*> allocations;
 

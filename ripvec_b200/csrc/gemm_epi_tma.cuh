@@ -1,0 +1,162 @@
+// Epilogue functors for the TMA-staged epilogue of the two-CTA GEMM (gemm_tc2_tma_kernel).
+//
+// The kernel moves data; the functor only computes.  For one output row and one group of 64
+// accumulator columns it receives v0 (columns col..col+31) and v1 (col+32..col+63) in f32 and,
+// when kReadsC, the 64 current values of the output row (the residual) already read from shared
+// memory; it leaves its kOutCols results in v0 (then v1).  The kernel packs them into the staging
+// tile and a single thread writes the tile with a TMA store, so the epilogue threads never wait
+// on global memory.
+#pragma once
+
+#include "gemm_ln_epi.cuh"
+
+namespace rv {
+
+__device__ __forceinline__ float gelu_tanh_fast(float x) { return gelu_tanh(x); }
+
+// x <- x + acc, then LayerNorm partials of the stored (rounded) row per 256-column tile.
+template <typename T>
+struct TEpiResidualStats {
+  float2* stats;
+  int stats_ld;
+  static constexpr int kOutCols = 64;
+  static constexpr bool kReadsC = true;
+  struct Tile {
+    float n, mean, m2;
+  };
+  __device__ __forceinline__ void stage(float*, int, int) {}
+  __device__ __forceinline__ void tile_load(Tile& t, int, int) const {
+    t.n = 0.f;
+    t.mean = 0.f;
+    t.m2 = 0.f;
+  }
+  __device__ __forceinline__ void compute(Tile& t, int row, int col, const float* r, float (&v0)[32],
+                                          float (&v1)[32], bool live) const {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float* v = (i < 4) ? &v0[8 * i] : &v1[8 * (i - 4)];
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[j] + r[8 * i + j];
+      unpack8<T>(pack8<T>(o), o);  // the values as they will be stored
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = o[j];
+      float m = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m += o[j];
+      m *= 0.125f;
+      float q = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q += (o[j] - m) * (o[j] - m);
+      const float tot = t.n + 8.f;
+      const float d = m - t.mean;
+      t.mean += d * (8.f / tot);
+      t.m2 += q + d * d * (t.n * 8.f / tot);
+      t.n = tot;
+    }
+    if (live && (col & 255) == 192)
+      stats[static_cast<size_t>(row) * stats_ld + (col >> 8)] = make_float2(t.mean, t.m2);
+  }
+};
+
+// Rotary embedding of the Q / K heads (columns < rope_cols), optionally after a folded LayerNorm.
+template <typename T, bool kNorm>
+struct TEpiQkv {
+  int rope_cols;
+  const int* pos;
+  const float* cos_t;
+  const float* sin_t;
+  LnFold ln;
+  float* cs_smem = nullptr;
+  static constexpr int kOutCols = 64;
+  static constexpr bool kReadsC = false;
+  struct Tile {
+    float4 cv[8], sv[8];
+    float mu, rstd;
+  };
+  __device__ __forceinline__ void stage(float* s, int t, int nt) {
+    if (kNorm) {
+      ln.stage_into(s, t, nt);
+      cs_smem = s;
+    }
+  }
+  __device__ __forceinline__ void tile_load(Tile& t, int row, int n0) const {
+    if (n0 < rope_cols) {
+      const int p = pos[row];
+      const float4* cs = reinterpret_cast<const float4*>(cos_t + static_cast<size_t>(p) * 32);
+      const float4* sn = reinterpret_cast<const float4*>(sin_t + static_cast<size_t>(p) * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        t.cv[i] = cs[i];
+        t.sv[i] = sn[i];
+      }
+    }
+    if (kNorm) row_stats(ln.stats + static_cast<size_t>(row) * ln.stats_ld, ln.stats_n, ln.eps, t.mu, t.rstd);
+  }
+  __device__ __forceinline__ void compute(Tile& t, int, int col, const float*, float (&v0)[32],
+                                          float (&v1)[32], bool) const {
+    if (kNorm) {
+      const float4* cs = reinterpret_cast<const float4*>(cs_smem + col);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 c0 = cs[i], c1 = cs[8 + i];
+        const float ca[4] = {c0.x, c0.y, c0.z, c0.w}, cb[4] = {c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v0[4 * i + j] = t.rstd * (v0[4 * i + j] - t.mu * ca[j]);
+          v1[4 * i + j] = t.rstd * (v1[4 * i + j] - t.mu * cb[j]);
+        }
+      }
+    }
+    if (col < rope_cols) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float cc[4] = {t.cv[i].x, t.cv[i].y, t.cv[i].z, t.cv[i].w};
+        const float ss[4] = {t.sv[i].x, t.sv[i].y, t.sv[i].z, t.sv[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float f = v0[4 * i + j], s = v1[4 * i + j];
+          v0[4 * i + j] = f * cc[j] - s * ss[j];
+          v1[4 * i + j] = f * ss[j] + s * cc[j];
+        }
+      }
+    }
+  }
+};
+
+// Folded LayerNorm, then GeGLU over the interleaved value (v0) / gate (v1) halves; the 32 results
+// are left in v0.
+template <typename T>
+struct TEpiNormGeglu {
+  LnFold ln;
+  float* cs_smem = nullptr;
+  static constexpr int kOutCols = 32;
+  static constexpr bool kReadsC = false;
+  struct Tile {
+    float mu, rstd;
+  };
+  __device__ __forceinline__ void stage(float* s, int t, int nt) {
+    ln.stage_into(s, t, nt);
+    cs_smem = s;
+  }
+  __device__ __forceinline__ void tile_load(Tile& t, int row, int) const {
+    row_stats(ln.stats + static_cast<size_t>(row) * ln.stats_ld, ln.stats_n, ln.eps, t.mu, t.rstd);
+  }
+  __device__ __forceinline__ void compute(Tile& t, int, int col, const float*, float (&v0)[32],
+                                          float (&v1)[32], bool) const {
+    const float4* cs = reinterpret_cast<const float4*>(cs_smem + col);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 c0 = cs[i], c1 = cs[8 + i];
+      const float ca[4] = {c0.x, c0.y, c0.z, c0.w}, cb[4] = {c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = t.rstd * (v0[4 * i + j] - t.mu * ca[j]);
+        const float g = t.rstd * (v1[4 * i + j] - t.mu * cb[j]);
+        v0[4 * i + j] = gelu_tanh_fast(a) * g;
+      }
+    }
+  }
+};
+
+}  // namespace rv

@@ -1,6 +1,7 @@
 // Instantiations of the tcgen05 GEMM for the epilogues the encoders use.
 #include "gemm_ln_epi.cuh"
 #include "gemm_tc2.cuh"
+#include "gemm_tc2_tma.cuh"
 #include "kernels.h"
 #include "tmap.h"
 
@@ -71,6 +72,27 @@ cudaError_t dispatch_epi(const GemmArgs& a, unsigned int* err, cudaStream_t st) 
 template <typename T>
 cudaError_t dispatch_pair(const GemmArgs& a, unsigned int* err, cudaStream_t st) {
   const int sms = device_sm_count();
+  if (a.tmC) {  // TMA-staged epilogue
+    switch (a.epi) {
+      case GemmEpi::kQkvRope:
+        return launch_gemm_tc2_tma<T>(*a.tmA, *a.tmB, *a.tmC, a.M, a.N, a.K,
+                                      TEpiQkv<T, false>{a.rope_cols, a.pos, a.cos_t, a.sin_t, make_fold(a)}, err,
+                                      sms, st);
+      case GemmEpi::kNormQkvRope:
+        return launch_gemm_tc2_tma<T>(*a.tmA, *a.tmB, *a.tmC, a.M, a.N, a.K,
+                                      TEpiQkv<T, true>{a.rope_cols, a.pos, a.cos_t, a.sin_t, make_fold(a)}, err,
+                                      sms, st);
+      case GemmEpi::kResidualStats:
+        return launch_gemm_tc2_tma<T>(*a.tmA, *a.tmB, *a.tmC, a.M, a.N, a.K,
+                                      TEpiResidualStats<T>{static_cast<float2*>(a.stats), a.stats_ld}, err, sms,
+                                      st);
+      case GemmEpi::kNormGeglu:
+        return launch_gemm_tc2_tma<T>(*a.tmA, *a.tmB, *a.tmC, a.M, a.N, a.K, TEpiNormGeglu<T>{make_fold(a)}, err,
+                                      sms, st);
+      default:
+        return cudaErrorInvalidValue;
+    }
+  }
   switch (a.epi) {
     case GemmEpi::kStore:
       return launch_gemm_tc2<T>(*a.tmA, *a.tmB, a.M, a.N, a.K, EpiStore<T>{static_cast<T*>(a.c), a.ldc}, err,

@@ -268,7 +268,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         epi.tile_load(tile, row, n0);
         epi.load(pre[0], row, n0);
       }
-      if (!mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag)) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag))) { ok = false; break; }
       tc_fence_after();
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * kBN);

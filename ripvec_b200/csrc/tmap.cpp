@@ -24,7 +24,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 bool make_tmap_2d_16bit(CUtensorMap* out, const void* base, bool is_bf16, uint64_t inner,
                         uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
-                        uint32_t box_outer, std::string* why) {
+                        uint32_t box_outer, std::string* why, int swizzle_bytes) {
   auto fn = encode_fn();
   if (!fn) {
     if (why) *why = "cuTensorMapEncodeTiled entry point unavailable";
@@ -40,7 +40,8 @@ bool make_tmap_2d_16bit(CUtensorMap* out, const void* base, bool is_bf16, uint64
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(out, is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                   2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     if (why) *why = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(int(r));

@@ -182,7 +182,7 @@ def test_safetensors_loading_matches_direct_upload(tiny_modern, tmp_path, dtype)
     np.testing.assert_array_equal(a, b)
 
 
-@pytest.mark.parametrize("env", ["RV_LN_FUSED", "RV_GEMM_2SM"])
+@pytest.mark.parametrize("env", ["RV_LN_FUSED", "RV_GEMM_2SM", "RV_TMA_EPI"])
 def test_kernel_variants_agree(base_weights, monkeypatch, env):
     """LayerNorm folded into the GEMMs vs separate LayerNorm kernels, and two-CTA vs one-CTA GEMM
     tiles: both variants of each pair must give the same embeddings (and match the oracle)."""
