@@ -169,7 +169,9 @@ int rv_index_topk_noalloc(rv_index* idx, const float* queries_dev, int32_t nq, i
  * 256 (one-CTA 128 x bn tiles) or 512 (two-CTA 256 x 256 tiles). */
 int rv_op_gemm(int32_t act_dtype, const void* a, const void* b, void* c, int32_t c_dtype,
                int32_t M, int32_t N, int32_t K, int32_t bn, void* stream);
-/* Attention over packed qkv [T, 3*heads*head_dim]; window_half < 0 = global. */
+/* Attention over packed qkv [T, 3*heads*head_dim]; window_half < 0 = global.  head_dim 64 runs
+ * the tcgen05 kernel (environment RV_ATTN_TC=0 selects the mma.sync kernel instead); head_dim
+ * 32 always runs the mma.sync kernel.  A pipeline wait that expires returns RV_E_DEVICE. */
 int rv_op_attention(int32_t act_dtype, const void* qkv, void* ctx_out, const int32_t* cu_seqlens_host,
                     int32_t n_seqs, int32_t num_heads, int32_t head_dim, int32_t window_half,
                     float scale, void* stream);

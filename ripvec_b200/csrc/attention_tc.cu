@@ -1,0 +1,620 @@
+// Varlen attention on the 5th-generation tensor cores (head_dim 64, bf16 or f16).
+//
+// Work item = (128-query tile of one sequence, head); the host lists the tiles as
+// {sequence start, length, first query} records.  The kernel is persistent: two CTAs per SM each
+// walk the items blockIdx.x, blockIdx.x + gridDim.x, ... (head-major, so the items in flight
+// share their sequences' K/V in L2), and every ring below runs across item boundaries, so the
+// next item's Q and K/V load while the current one finishes.  Warp roles (192 threads):
+//   warp 0      TMA producer: Q per item (2 buffers), K tiles (2-deep ring) and V tiles (3-deep)
+//               of 64 keys,
+//   warp 1      TMEM owner and single-thread tcgen05.mma issuer,
+//   warps 2..5  softmax: thread r owns query row r (= TMEM lane r).
+// Per key tile g (counted across items):
+//   S[g&1] = Q K^T      tcgen05.mma M=128 N=64 K=64 into TMEM, issued two tiles ahead,
+//   softmax             each thread reads its 64 scores with tcgen05.ld, masks keys past the
+//                       sequence end and, on sliding-window layers, keys with |i - j| > w/2;
+//                       keeps the running max and sum in f32 and writes P = exp2(s - m) as
+//                       16-bit into a 128-byte-swizzled shared tile.  32-key halves that no row
+//                       of the warp can see skip the exponentials,
+//   O[g&1] = P V        tcgen05.mma M=128 N=64 K=64 with V as an MN-major operand,
+//   accumulate          O_reg = O_reg * alpha + O[g&1] in registers, one tile behind, so the
+//                       P V MMA overlaps the next tile's softmax; the last fold of an item
+//                       writes its context rows.
+// Reference semantics: backend/arch/modern_bert.rs:250-322 and driver/cpu.rs:1016-1074 (scores *
+// 1/sqrt(d), additive -1e9 masks for padding and |i-j| > window/2, max-subtracted softmax, P V);
+// masked keys get weight 0 exactly, as exp(-1e9 - max) does in f32.
+#include "common.cuh"
+#include "kernels.h"
+#include "tmap.h"
+
+namespace rv {
+
+namespace {
+
+constexpr int kBQ = 128;       // queries per item
+constexpr int kBKV = 64;       // keys per tile
+constexpr int kD = 64;         // head dim
+constexpr int kKStages = 2;
+constexpr int kVStages = 3;
+constexpr int kQBytes = kBQ * kD * 2;    // 16 KB
+constexpr int kKVBytes = kBKV * kD * 2;  // 8 KB
+constexpr int kPBytes = kBQ * kBKV * 2;  // 16 KB
+constexpr int kTmemCols = 256;           // S[2] at columns 0, 64; O[2] at 128, 192
+constexpr int kThreads = 320;  // producer, MMA issuer, 8 softmax warps
+// Row-max / row-sum exchange between the two softmax warps of a row: max [2 tiles][2 halves][128]
+// and sum [2 items][2 halves][128] floats.
+constexpr int kXBytes = (2 * 2 * kBQ + 2 * 2 * kBQ) * 4;
+// 110 KB: two CTAs fit an SM and a third never does, so 2 x 256 TMEM columns always fit.
+constexpr int kSmem =
+    1024 + 2 * kQBytes + (kKStages + kVStages) * kKVBytes + 2 * kPBytes + kXBytes + 512;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Shared-memory descriptor of an MN-major operand tile written by TMA with 128-byte swizzling:
+// rows of 64 16-bit elements along N (128 B), 8-row swizzle atoms of 1024 B stacked along K.
+// The stride between 8-row K groups is 1024 B; the tile is a single 64-wide N block, so the
+// N-block stride is never used and is given the same value (every address the descriptor can
+// form stays inside the 8 KB tile).
+__device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1024u >> 4) << 16;   // leading byte offset
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;   // stride byte offset (8-row K groups)
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Completion wait that ignores the abort flag (bounded by time only): used on error paths to let
+// copies and MMAs already in flight finish before the CTA releases its memory.
+__device__ __forceinline__ bool wait_done(uint64_t* bar, uint32_t parity) {
+  volatile int no_abort = 0;
+  return mbar_wait(bar, parity, &no_abort);
+}
+
+__host__ __device__ constexpr uint32_t idesc_f16_bmn(int M, int N, bool is_bf16) {
+  return idesc_f16(M, N, is_bf16) | (1u << 16);  // B operand MN-major
+}
+
+__device__ __forceinline__ uint32_t swz128(int r, int j) {
+  return static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
+}
+
+
+// Barrier of the two softmax warps of a row (named barrier `id`, 64 threads) that also ORs a
+// flag over them, so a wait that failed in either warp ends both at the same point.
+__device__ __forceinline__ bool pair_any(int id, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, 64, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(static_cast<int>(pred)), "r"(id)
+      : "memory");
+  return r != 0;
+}
+
+// Class of 32 keys [kb, kb + 31] for the 32 queries [qa, qb] of one warp: 0 = visible to none of
+// them, 2 = every key visible to every query, 1 = mask per element.
+__device__ __forceinline__ int half_class(int kb, int L, int qa, int qb, int wh) {
+  const int ke = kb + 31;
+  if (kb >= L) return 0;
+  if (wh < 0) return ke < L ? 2 : 1;
+  if (ke < qa - wh || kb > qb + wh) return 0;
+  return (ke < L && kb >= qb - wh && ke <= qa + wh) ? 2 : 1;
+}
+
+// Packed f32x2 arithmetic (one instruction for two lanes of a 64-bit register pair) and the
+// three-input max of sm_100.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Masks (class 1) the 32 scores of keys kb..kb+31 for query qi to -inf and returns their max.
+__device__ __forceinline__ float masked_max(float (&s)[32], int cls, int kb, int L, int qi, int wh) {
+  if (cls == 1) {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      const int k = kb + c;
+      const bool vis = k < L && (wh < 0 || abs(qi - k) <= wh);
+      if (!vis) s[c] = -INFINITY;
+    }
+  }
+  float mx[4] = {fmax3(s[0], s[1], s[2]), fmax3(s[3], s[4], s[5]), fmax3(s[6], s[7], s[8]),
+                 fmax3(s[9], s[10], s[11])};
+#pragma unroll
+  for (int c = 12; c < 32; c += 2) mx[(c >> 1) & 3] = fmax3(mx[(c >> 1) & 3], s[c], s[c + 1]);
+  return fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
+}
+
+// P = exp2(s * scale_log2 - m) of 32 keys as 16-bit, into 16-byte chunks c8_0..c8_0+3 of row r
+// of the swizzled P tile (zeros when the half is not visible); adds the f32 values to the two
+// packed partial sums ps.  sl2 = {scale_log2, scale_log2}, nm2 = {-m, -m}.
+template <typename T>
+__device__ __forceinline__ void write_p(uint8_t* pt, int r, int c8_0, bool live, const float (&s)[32],
+                                        uint64_t sl2, uint64_t nm2, uint64_t (&ps)[2]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t w4[4] = {0u, 0u, 0u, 0u};
+    if (live) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        // Masked scores are -inf: exp2(-inf) = 0 exactly.
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(s[8 * c + 2 * e], s[8 * c + 2 * e + 1]), sl2, nm2), x0, x1);
+        const float p0 = ex2(x0), p1 = ex2(x1);
+        ps[e & 1] = f2_add(ps[e & 1], f2_pack(p0, p1));
+        auto v = Elem<T>::pack(p0, p1);
+        w4[e] = *reinterpret_cast<uint32_t*>(&v);
+      }
+    }
+    *reinterpret_cast<uint4*>(pt + swz128(r, c8_0 + c)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  }
+}
+
+// The (item, key tile) sequence one CTA processes: items w = blockIdx.x + k * gridDim.x; item w
+// is query tile w % n_tiles of head w / n_tiles.  The launch constants (tiles, n_tiles, n_items,
+// window) stay in the parameter bank; the next item's record is loaded one item ahead so its
+// latency overlaps the current item.
+struct Walk {
+  int w;  // current item (done when >= n_items)
+  int i;  // ordinal of the item within this CTA
+  int j;  // key tile within the item
+  int s0, L, q0, t_lo, n_kv;
+  int2 nxt;
+
+  __device__ __forceinline__ static int2 load(const int2* tiles, int n_tiles, int item) {
+    return __ldg(&tiles[item - (item / n_tiles) * n_tiles]);
+  }
+  __device__ __forceinline__ int head(int n_tiles) const { return w / n_tiles; }
+  __device__ __forceinline__ void set(int2 rec, int wh) {
+    s0 = rec.x;
+    L = rec.y & 0xFFFF;
+    q0 = rec.y >> 16;
+    int kv_lo = 0, kv_hi = L;
+    if (wh >= 0) {
+      kv_lo = max(0, q0 - wh);
+      kv_hi = min(L, q0 + kBQ + wh);
+    }
+    t_lo = kv_lo / kBKV;
+    n_kv = (kv_hi + kBKV - 1) / kBKV - t_lo;  // >= 1 because q0 < L
+  }
+  __device__ __forceinline__ void init(const int2* tiles, int n_tiles, int n_items, int wh) {
+    w = blockIdx.x;
+    i = 0;
+    j = 0;
+    if (w < n_items) {
+      set(load(tiles, n_tiles, w), wh);
+      if (w + static_cast<int>(gridDim.x) < n_items) nxt = load(tiles, n_tiles, w + gridDim.x);
+    }
+  }
+  __device__ __forceinline__ bool valid(int n_items) const { return w < n_items; }
+  __device__ __forceinline__ bool last_tile() const { return j == n_kv - 1; }
+  __device__ __forceinline__ void next(const int2* tiles, int n_tiles, int n_items, int wh) {
+    if (++j < n_kv) return;
+    j = 0;
+    ++i;
+    w += gridDim.x;
+    if (w < n_items) {
+      set(nxt, wh);
+      if (w + static_cast<int>(gridDim.x) < n_items) nxt = load(tiles, n_tiles, w + gridDim.x);
+    }
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_constant__ CUtensorMap tmQKV,
+                                                              T* __restrict__ ctx,
+                                                              const int2* __restrict__ tiles,
+                                                              int n_tiles, int n_items, int H,
+                                                              int window_half, float scale_log2,
+                                                              unsigned int* err) {
+  constexpr bool kBf = Elem<T>::kBf16;
+  constexpr uint32_t kIdS = idesc_f16(kBQ, kBKV, kBf);
+  constexpr uint32_t kIdO = idesc_f16_bmn(kBQ, kD, kBf);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;                        // [2] x 16 KB
+  uint8_t* sK = sQ + 2 * kQBytes;            // [kKStages] x 8 KB
+  uint8_t* sV = sK + kKStages * kKVBytes;    // [kVStages] x 8 KB
+  uint8_t* sP = sV + kVStages * kKVBytes;    // [2] x 16 KB
+  float* xmax = reinterpret_cast<float*>(sP + 2 * kPBytes);  // [2][2][kBQ]
+  float* xsum = xmax + 2 * 2 * kBQ;                           // [2][2][kBQ]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(xsum + 2 * 2 * kBQ);
+  uint64_t* q_full = bar;          // [2] Q landed
+  uint64_t* q_empty = bar + 2;     // [2] last S MMA of the item that read Q completed
+  uint64_t* k_full = bar + 4;      // [kKStages]
+  uint64_t* k_empty = bar + 6;     // [kKStages] S MMA that read the K tile completed
+  uint64_t* v_full = bar + 8;      // [kVStages]
+  uint64_t* v_empty = bar + 11;    // [kVStages] P V MMA that read the V tile completed
+  uint64_t* s_full = bar + 14;     // [2] scores in TMEM
+  uint64_t* p_full = bar + 16;     // [2] P written (and the scores read) by the 8 softmax warps
+  uint64_t* p_empty = bar + 18;    // [2] P V MMA of the tile completed (P slot free, O updated)
+  uint64_t* o_empty = bar + 20;    // [2] an item's O read out by the 8 softmax warps
+  uint64_t* drain = bar + 22;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 25);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&q_full[b], 1);
+      mbar_init(&q_empty[b], 1);
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 8);
+      mbar_init(&p_empty[b], 1);
+      mbar_init(&o_empty[b], 8);
+    }
+    for (int b = 0; b < kKStages; ++b) {
+      mbar_init(&k_full[b], 1);
+      mbar_init(&k_empty[b], 1);
+    }
+    for (int b = 0; b < kVStages; ++b) {
+      mbar_init(&v_full[b], 1);
+      mbar_init(&v_empty[b], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQKV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  static_assert(kKStages == 2 && kVStages == 3, "barrier offsets assume 2 K and 3 V stages");
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      Walk wk;
+      wk.init(tiles, n_tiles, n_items, window_half);
+      bool ok = true;
+      // Per-slot record of issued loads (bit = slot issued, parity of its last phase), so that an
+      // aborting CTA can let them land before it exits.
+      uint32_t q_iss = 0, q_par = 0, k_iss = 0, k_par = 0, v_iss = 0, v_par = 0;
+      int ks = 0, vs = 0;
+      uint32_t kph = 0, vph = 0;
+      while (wk.valid(n_items)) {
+        if (wk.j == 0) {
+          const int qs = wk.i & 1;
+          const uint32_t qph = (wk.i >> 1) & 1;
+          if (!mbar_wait(&q_empty[qs], qph ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&q_full[qs], kQBytes);
+          tma_load_2d(sQ + qs * kQBytes, &tmQKV, &q_full[qs], wk.head(n_tiles) * kD, wk.s0 + wk.q0);
+          tma_load_2d(sQ + qs * kQBytes + kQBytes / 2, &tmQKV, &q_full[qs], wk.head(n_tiles) * kD,
+                      wk.s0 + wk.q0 + kBQ / 2);
+          q_iss |= 1u << qs;
+          q_par = (q_par & ~(1u << qs)) | (qph << qs);
+        }
+        const int row = wk.s0 + (wk.t_lo + wk.j) * kBKV;
+        if (!mbar_wait(&k_empty[ks], kph ^ 1u, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&k_full[ks], kKVBytes);
+        tma_load_2d(sK + ks * kKVBytes, &tmQKV, &k_full[ks], H + wk.head(n_tiles) * kD, row);
+        k_iss |= 1u << ks;
+        k_par = (k_par & ~(1u << ks)) | (kph << ks);
+        if (++ks == kKStages) { ks = 0; kph ^= 1u; }
+        if (!mbar_wait(&v_empty[vs], vph ^ 1u, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&v_full[vs], kKVBytes);
+        tma_load_2d(sV + vs * kKVBytes, &tmQKV, &v_full[vs], 2 * H + wk.head(n_tiles) * kD, row);
+        v_iss |= 1u << vs;
+        v_par = (v_par & ~(1u << vs)) | (vph << vs);
+        if (++vs == kVStages) { vs = 0; vph ^= 1u; }
+        wk.next(tiles, n_tiles, n_items, window_half);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(err, kErrWaitTimeout);
+        for (int b = 0; b < 2; ++b)
+          if (q_iss & (1u << b)) wait_done(&q_full[b], (q_par >> b) & 1u);
+        for (int b = 0; b < kKStages; ++b)
+          if (k_iss & (1u << b)) wait_done(&k_full[b], (k_par >> b) & 1u);
+        for (int b = 0; b < kVStages; ++b)
+          if (v_iss & (1u << b)) wait_done(&v_full[b], (v_par >> b) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      Walk ws, wp;  // S runs two tiles ahead of P V
+      ws.init(tiles, n_tiles, n_items, window_half);
+      wp.init(tiles, n_tiles, n_items, window_half);
+      int ks = 0, vs = 0;
+      uint32_t kph = 0, vph = 0, gs = 0, gp = 0;
+      // S[gs & 1] = Q K^T over the 64-wide head dim (4 MMAs of K = 16).  S[gs & 1] is free: the
+      // softmax warps released S of tile gs - 2 (p_full) before P V of that tile was issued.
+      auto issue_s = [&]() -> bool {
+        const int qs = ws.i & 1;
+        if (ws.j == 0 && !mbar_wait(&q_full[qs], (ws.i >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait(&k_full[ks], kph, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + qs * kQBytes);
+        const uint32_t k_addr = smem_u32(sK + ks * kKVBytes);
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          tc_mma_f16(tmem_base + (gs & 1) * kBKV, smem_desc_sw128(q_addr + 32 * kk),
+                     smem_desc_sw128(k_addr + 32 * kk), kIdS, kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[gs & 1]);
+        tc_commit(&k_empty[ks]);
+        if (ws.last_tile()) tc_commit(&q_empty[qs]);
+        if (++ks == kKStages) { ks = 0; kph ^= 1u; }
+        ++gs;
+        ws.next(tiles, n_tiles, n_items, window_half);
+        return true;
+      };
+      bool ok = true;
+      if (ws.valid(n_items)) ok = issue_s();
+      if (ok && ws.valid(n_items)) ok = issue_s();
+      while (ok && wp.valid(n_items)) {
+        const int b = gp & 1;
+        const uint32_t ph = (gp >> 1) & 1;
+        const int os = wp.i & 1;  // O buffer of the item
+        // O[os] (+)= P V: P is K-major over the 64 keys, V is MN-major (keys x head dim).  An
+        // item's first tile overwrites O[os], once the item two back has been read out of it.
+        if ((wp.j == 0 && !mbar_wait(&o_empty[os], ((wp.i >> 1) & 1) ^ 1u, abort_flag)) ||
+            !mbar_wait(&p_full[b], ph, abort_flag) || !mbar_wait(&v_full[vs], vph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(sP + b * kPBytes);
+        const uint32_t v_addr = smem_u32(sV + vs * kKVBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBKV / 16; ++kk)
+          tc_mma_f16(tmem_base + 2 * kBKV + os * kD, smem_desc_sw128(p_addr + 32 * kk),
+                     smem_desc_sw128_mn(v_addr + 2048 * kk), kIdO, (wp.j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&v_empty[vs]);
+        tc_commit(&p_empty[b]);
+        if (++vs == kVStages) { vs = 0; vph ^= 1u; }
+        ++gp;
+        wp.next(tiles, n_tiles, n_items, window_half);
+        if (ws.valid(n_items)) ok = issue_s();
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(err, kErrWaitTimeout);
+      }
+      // Every MMA this thread issued completes before TMEM is released.
+      tc_commit(drain);
+      if (!wait_done(drain, 0)) atomicOr(err, kErrWaitTimeout);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax
+    // Warp w (2..9) owns TMEM lanes of quadrant w % 4 and the 32 keys (and 32 O columns) of half
+    // (w - 2) / 4 of each tile; warps w and w + 4 share their rows through xmax / xsum.
+    const int half = (warp - 2) >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // query row of the item (= TMEM lane)
+    const int pair_id = 1 + quad;    // named barrier of the two warps of these rows
+    const uint32_t trow = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    Walk wk;
+    wk.init(tiles, n_tiles, n_items, window_half);
+    // Reference max m (log2 units, kNone until a key is visible) and this half's sum l of the row
+    // for the current item.  P = exp2(s - m) accumulates into the item's O in TMEM; m only moves
+    // when a tile's max exceeds it by more than kRescale (then O and l are rescaled), so P stays
+    // <= 2^kRescale.  Both halves of a row apply the same updates to m.
+    constexpr float kRescale = 8.f;
+    constexpr float kNone = -1e30f;
+    float m = kNone, l = 0.f;
+    // The finished item whose context row is written after the next item's first tile, so its
+    // last P V MMA completes behind that tile's softmax.
+    bool fin = false, fin_live = false;
+    int fin_slot = 0, fin_b = 0;
+    uint32_t fin_ph = 0, fin_off = 0;  // fin_off: element offset (T * H < 2^31, host-checked)
+    uint32_t g = 0;
+    bool fail = false;  // a wait of this thread expired or another role aborted
+
+    for (;;) {
+      const bool have = wk.valid(n_items);
+      const int b = g & 1;
+      const uint32_t ph = (g >> 1) & 1;
+      const int qi = wk.q0 + r;
+      int cls = 0;
+      float sv[32];
+      if (have) {
+        if (wk.j == 0) {
+          m = kNone;
+          l = 0.f;
+        }
+        const int qa = wk.q0 + quad * 32;
+        const int kb = (wk.t_lo + wk.j) * kBKV + 32 * half;
+        cls = half_class(kb, wk.L, qa, qa + 31, window_half);
+        // Every warp waits for every tile's scores, so the phases it tracks never fall behind.
+        fail = fail || !__all_sync(0xffffffffu, mbar_wait(&s_full[b], ph, abort_flag));
+        // P slot b is free once the P V MMA of tile g - 2 completed (almost always already true).
+        fail = fail || !__all_sync(0xffffffffu, mbar_wait(&p_empty[b], ph ^ 1u, abort_flag));
+        float mt = -INFINITY;
+        if (!fail && cls) {
+          tc_fence_after();
+          tmem_ld32(trow + b * kBKV + 32 * half, sv);
+          tc_wait_ld();
+          mt = masked_max(sv, cls, kb, wk.L, qi, window_half) * scale_log2;
+        }
+        xmax[((g & 1) * 2 + half) * kBQ + r] = mt;
+      }
+      // Exchange the half-row maxima (and any failure) with the partner warp.
+      if (pair_any(pair_id, fail)) break;
+      if (have) {
+        const float mt = fmaxf(xmax[((g & 1) * 2 + half) * kBQ + r], xmax[((g & 1) * 2 + (half ^ 1)) * kBQ + r]);
+        // A row that has seen no key yet (its O row is 0) adopts the tile's max; a row whose max
+        // grew by more than kRescale rescales its O and l (rare: the warp waits for the previous
+        // P V into O, then reads, scales and rewrites its 32 lanes x 32 columns).
+        const bool need = m != kNone && mt > m + kRescale;
+        if (m == kNone) m = fmaxf(m, mt);
+        if (__any_sync(0xffffffffu, need)) {
+          fail = !__all_sync(0xffffffffu, mbar_wait(&p_empty[b ^ 1], ((g - 1) >> 1) & 1, abort_flag));
+          if (!fail) {
+            tc_fence_after();
+            const float alpha = need ? ex2(m - mt) : 1.f;
+            const uint32_t ocol = trow + 2 * kBKV + (wk.i & 1) * kD + 32 * half;
+            float t[32];
+            tmem_ld32(ocol, t);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] *= alpha;
+            tmem_st32(ocol, t);
+            tc_wait_st();
+            if (need) {
+              l *= alpha;
+              m = mt;
+            }
+          }
+        }
+        if (!fail) {
+          uint8_t* pt = sP + b * kPBytes;
+          const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m, -m);
+          uint64_t ps[2] = {0ull, 0ull};  // two packed partial sums (f32 zero bits)
+          write_p<T>(pt, r, 4 * half, cls != 0, sv, sl2, nm2, ps);
+          float p0, p1, p2, p3;
+          f2_unpack(ps[0], p0, p1);
+          f2_unpack(ps[1], p2, p3);
+          l += (p0 + p1) + (p2 + p3);
+          fence_async_smem();  // generic-proxy stores -> visible to the tensor core
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_full[b]);
+        }
+      }
+      if (fin) {
+        // Context row = O / (l_half0 + l_half1), read from TMEM once the item's last P V
+        // completed (p_empty of its slot); then O[fin_slot] is released for the item two ahead.
+        fail = fail || !__all_sync(0xffffffffu, mbar_wait(&p_empty[fin_b], fin_ph, abort_flag));
+        if (pair_any(pair_id, fail)) break;
+        const float lt = xsum[(fin_slot * 2) * kBQ + r] + xsum[(fin_slot * 2 + 1) * kBQ + r];
+        const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+        tc_fence_after();
+        float t[32];
+        tmem_ld32(trow + 2 * kBKV + fin_slot * kD + 32 * half, t);
+        tc_wait_ld();
+        if (fin_live) {
+          uint4* dst = reinterpret_cast<uint4*>(ctx + fin_off + 32 * half);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = t[8 * c + e] * inv;
+            dst[c] = pack8<T>(f);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_empty[fin_slot]);
+        fin = false;
+      }
+      if (!have) break;
+      if (wk.last_tile()) {
+        fin = true;
+        fin_live = qi < wk.L;
+        fin_slot = wk.i & 1;
+        fin_b = b;
+        fin_ph = ph;
+        fin_off = static_cast<uint32_t>((wk.s0 + qi) * H + wk.head(n_tiles) * kD);
+        xsum[(fin_slot * 2 + half) * kBQ + r] = l;
+      }
+      ++g;
+      wk.next(tiles, n_tiles, n_items, window_half);
+    }
+    if (fail && lane == 0) {
+      *abort_flag = 1;
+      atomicOr(err, kErrWaitTimeout);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <typename T>
+cudaError_t launch_attn_tc(const CUtensorMap& tm, void* ctx, const int2* tiles, int n_tiles,
+                           int num_heads, int window_half, float scale, unsigned int* err,
+                           cudaStream_t st) {
+  static bool attr_set[64] = {false};  // the attribute is per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int n_items = n_tiles * num_heads;
+  const int slots = 2 * device_sm_count();
+  const int grid = n_items < slots ? n_items : slots;
+  const float scale_log2 = scale * 1.4426950408889634f;
+  attn_tc_kernel<T><<<grid, kThreads, kSmem, st>>>(tm, static_cast<T*>(ctx), tiles, n_tiles, n_items,
+                                                   num_heads * kD, window_half, scale_log2, err);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t attention_varlen_tc(Act act, const void* qkv, void* ctx, int total_tokens,
+                                const int2* tiles, int n_tiles, int num_heads, int window_half,
+                                float scale, unsigned int* err, cudaStream_t st) {
+  if (n_tiles <= 0 || total_tokens <= 0) return cudaSuccess;
+  if (int64_t(n_tiles) * num_heads > INT32_MAX ||
+      int64_t(total_tokens) * num_heads * kD > INT32_MAX)
+    return cudaErrorInvalidValue;
+  const int H = num_heads * kD;
+  // Rows past the batch read as zeros (TMA out-of-bounds fill), so the last sequence's ragged
+  // key tile never sees stale workspace contents.
+  CUtensorMap tm;
+  if (!make_tmap_2d_16bit(&tm, qkv, act == Act::kBf16, uint64_t(3) * H, uint64_t(total_tokens),
+                          uint64_t(3) * H * 2, 64, 64, nullptr))
+    return cudaErrorInvalidValue;
+  if (act == Act::kBf16)
+    return launch_attn_tc<__nv_bfloat16>(tm, ctx, tiles, n_tiles, num_heads, window_half, scale, err, st);
+  return launch_attn_tc<__half>(tm, ctx, tiles, n_tiles, num_heads, window_half, scale, err, st);
+}
+
+int fill_attention_tiles(const int* cu_seqlens, int n_seqs, int2* out) {
+  int t = 0;
+  for (int b = 0; b < n_seqs; ++b) {
+    const int s0 = cu_seqlens[b], L = cu_seqlens[b + 1] - s0;
+    if (L < 0 || L > kMaxAttnSeq) return -1;
+    for (int q0 = 0; q0 < L; q0 += kBQ) out[t++] = make_int2(s0, L | (q0 << 16));
+  }
+  return t;
+}
+
+}  // namespace rv

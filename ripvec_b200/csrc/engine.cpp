@@ -438,11 +438,16 @@ int alloc_workspaces(rv_ctx* c) {
   c->pos_d = static_cast<int*>(dalloc(c, size_t(T) * 4));
   c->meta_d = static_cast<int*>(dalloc(c, size_t(2) * (c->n_max + 1) * 4));
   c->out_d = static_cast<float*>(dalloc(c, size_t(c->n_max) * H * 4));
+  // A batch has at most t_max / 128 + n_max 128-query tiles.
+  c->tiles_cap = c->t_max / 128 + c->n_max + 1;
+  c->tiles_d = static_cast<int2*>(dalloc(c, size_t(c->tiles_cap) * sizeof(int2)));
   if (!c->x || !c->hn || !c->qkv || !c->cbuf || !c->act || !c->ids_d || !c->pos_d || !c->meta_d ||
-      !c->out_d)
+      !c->out_d || !c->tiles_d)
     return fail(c, RV_E_NOMEM, "workspace allocation failed");
   if (cudaMallocHost(reinterpret_cast<void**>(&c->meta_h), size_t(2) * (c->n_max + 1) * 4) !=
-      cudaSuccess)
+          cudaSuccess ||
+      cudaMallocHost(reinterpret_cast<void**>(&c->tiles_h), size_t(c->tiles_cap) * sizeof(int2)) !=
+          cudaSuccess)
     return fail(c, RV_E_NOMEM, "pinned staging allocation failed");
   if (cudaEventCreateWithFlags(&c->meta_evt, cudaEventDisableTiming) != cudaSuccess)
     return fail(c, RV_E_CUDA, "event creation failed");
@@ -493,14 +498,21 @@ int gemm(rv_ctx* c, const CUtensorMap& A, const rv::DeviceMatrix& B, int M, Gemm
 
 // One forward over a packed batch already on the device: ids (T tokens), meta_d holding
 // cu_seqlens and q-tile starts for n sequences.  Writes f32 embeddings to out [n, hidden].
-int forward(rv_ctx* c, const int* ids, int T, int n, int total_q_tiles, double pairs_global,
-            double pairs_local, float* out) {
+int forward(rv_ctx* c, const int* ids, int T, int n, int total_q_tiles, int total_q_tiles128,
+            double pairs_global, double pairs_local, float* out) {
   const int H = c->d.hidden, heads = c->d.num_heads, hd = H / heads;
   const int* cu = c->meta_d;
   const int* qts = c->meta_d + (n + 1);
   cudaStream_t st = c->stream;
   RV_LAUNCH_K(c, RV_KIND_EMBED, 0, rv::build_positions(cu, n, T, c->pos_d, st));
   const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+  auto attend = [&](int window_half) {
+    return c->attn_tc && hd == 64
+               ? rv::attention_varlen_tc(c->adt, c->qkv, c->cbuf, T, c->tiles_d, total_q_tiles128, heads,
+                                         window_half, scale, c->d_err, st)
+               : rv::attention_varlen(c->adt, c->qkv, c->cbuf, cu, qts, n, total_q_tiles, heads, hd,
+                                      window_half, scale, st);
+  };
   if (is_modern(c)) {
     RV_LAUNCH_K(c, RV_KIND_EMBED, 0, rv::embed_ln(c->adt, ids, T, c->tok_emb, c->d.vocab, c->emb_norm_w, nullptr,
                               nullptr, nullptr, nullptr, H, c->d.norm_eps, c->x, c->d_err, st));
@@ -522,8 +534,7 @@ int forward(rv_ctx* c, const int* ids, int T, int n, int total_q_tiles, double p
           return rc;
         }
         RV_LAUNCH_K(c, RV_KIND_ATTENTION, 4.0 * H * (lw.is_global ? pairs_global : pairs_local),
-                    rv::attention_varlen(c->adt, c->qkv, c->cbuf, cu, qts, n, total_q_tiles, heads, hd, wh,
-                                         scale, st));
+                    attend(wh));
         if ((rc = gemm(c, c->map_c, lw.wo, T, GemmEpi::kResidualStats, c->x, H, nullptr, 0, nullptr, nullptr,
                        c->stats_a)))
           return rc;
@@ -542,8 +553,7 @@ int forward(rv_ctx* c, const int* ids, int T, int n, int total_q_tiles, double p
                      3 * H, nullptr, 2 * H, c->rope_cos[g], c->rope_sin[g])))
         return rc;
       RV_LAUNCH_K(c, RV_KIND_ATTENTION, 4.0 * H * (lw.is_global ? pairs_global : pairs_local),
-                  rv::attention_varlen(c->adt, c->qkv, c->cbuf, cu, qts, n, total_q_tiles, heads, hd, wh,
-                                       scale, st));
+                  attend(wh));
       if ((rc = gemm(c, c->map_c, lw.wo, T, GemmEpi::kResidual, c->x, H))) return rc;
       RV_LAUNCH_K(c, RV_KIND_NORM, 0, rv::layernorm(c->adt, c->x, c->hn, T, H, lw.mlp_norm, nullptr,
                                                     c->d.norm_eps, st));
@@ -562,8 +572,7 @@ int forward(rv_ctx* c, const int* ids, int T, int n, int total_q_tiles, double p
       int rc;
       if ((rc = gemm(c, c->map_x, lw.wqkv, T, GemmEpi::kBias, c->qkv, 3 * H, lw.bqkv))) return rc;
       RV_LAUNCH_K(c, RV_KIND_ATTENTION, 4.0 * H * pairs_global,
-                  rv::attention_varlen(c->adt, c->qkv, c->cbuf, cu, qts, n, total_q_tiles, heads, hd,
-                                       -1, scale, st));
+                  attend(-1));
       if ((rc = gemm(c, c->map_c, lw.wo, T, GemmEpi::kResidual, c->x, H, lw.bo))) return rc;
       RV_LAUNCH_K(c, RV_KIND_NORM, 0, rv::layernorm(c->adt, c->x, c->x, T, H, lw.ln1_w, lw.ln1_b, c->d.norm_eps, st));
       if ((rc = gemm(c, c->map_x, lw.wi, T, GemmEpi::kBiasGelu, c->act, c->d.intermediate, lw.b1)))
@@ -646,10 +655,16 @@ int run_batches(rv_ctx* c, const int32_t* cu, int32_t n, IdsFn ids_src, OutFn ou
     }
     RV_CUDA_TRY(c, cudaMemcpyAsync(c->meta_d, mh, sizeof(int) * 2 * (nb + 1),
                                    cudaMemcpyHostToDevice, c->stream));
+    // 128-query tile records of the tcgen05 attention kernel.
+    const int n_tiles128 = rv::fill_attention_tiles(mh, nb, c->tiles_h);
+    if (n_tiles128 < 0) return fail(c, RV_E_INVALID, "sequence too long for the attention tiles");
+    if (n_tiles128 > 0)
+      RV_CUDA_TRY(c, cudaMemcpyAsync(c->tiles_d, c->tiles_h, sizeof(int2) * n_tiles128,
+                                     cudaMemcpyHostToDevice, c->stream));
     RV_CUDA_TRY(c, cudaEventRecord(c->meta_evt, c->stream));
     const int* ids = ids_src(b0, static_cast<int>(tokens));
     if (!ids) return RV_E_CUDA;
-    int rc = forward(c, ids, static_cast<int>(tokens), nb, q, pg, pl, c->out_d);
+    int rc = forward(c, ids, static_cast<int>(tokens), nb, q, n_tiles128, pg, pl, c->out_d);
     if (rc) return rc;
     if ((rc = out_dst(b0, nb, c->out_d))) return rc;
     b0 = b1;
@@ -690,9 +705,12 @@ int rv_create(const rv_model_desc* desc, int device, rv_ctx** out) {
   if (const char* e = std::getenv("RV_GEMM_2SM")) c->gemm_pair = std::strcmp(e, "0") != 0;
   if (const char* e = std::getenv("RV_LN_FUSED")) c->ln_fused = std::strcmp(e, "0") != 0;
   if (const char* e = std::getenv("RV_TMA_EPI")) c->tma_epi = std::strcmp(e, "0") != 0;
+  if (const char* e = std::getenv("RV_ATTN_TC")) c->attn_tc = std::strcmp(e, "0") != 0;
   c->t_max = d.max_batch_tokens > 0 ? d.max_batch_tokens : 262144;
   if (c->t_max < d.max_position) c->t_max = d.max_position;
   c->n_max = 65536;
+  // The tcgen05 attention addresses the context with 32-bit element offsets.
+  if (c->t_max * int64_t(d.hidden) > INT32_MAX) c->attn_tc = false;
   if (cudaSetDevice(device) != cudaSuccess) return RV_E_CUDA;
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return RV_E_CUDA;
   c->d_err = static_cast<unsigned int*>(dalloc(c.get(), 4));
@@ -708,6 +726,7 @@ void rv_destroy(rv_ctx* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (void* p : c->allocations) cudaFree(p);
     if (c->meta_h) cudaFreeHost(c->meta_h);
+    if (c->tiles_h) cudaFreeHost(c->tiles_h);
     if (c->meta_evt) cudaEventDestroy(c->meta_evt);
     for (auto& m : c->marks) {
       cudaEventDestroy(m.a);

@@ -87,13 +87,17 @@ struct rv_ctx {
   void* stats_b = nullptr;  // ... and after the MLP block
   int* ids_d = nullptr;
   int* pos_d = nullptr;
-  int* meta_d = nullptr;  // cu_seqlens (n_max+1) then q-tile starts (n_max+1)
+  int* meta_d = nullptr;  // cu_seqlens (n_max+1) then 64-query tile starts (n_max+1)
+  int2* tiles_d = nullptr; // 128-query tile records of the tcgen05 attention (tiles_cap)
+  int2* tiles_h = nullptr; // pinned staging of tiles_d
+  int64_t tiles_cap = 0;
   float* out_d = nullptr; // [n_max, hidden]
   int* meta_h = nullptr;  // pinned staging of meta_d
   cudaEvent_t meta_evt = nullptr;
   CUtensorMap map_x, map_hn, map_c, map_act;
   CUtensorMap map_qkv_out, map_act_out;  // TMA-staged epilogue outputs (x uses map_x)
   bool tma_epi = true;                   // TMA-staged GEMM epilogues (RV_TMA_EPI=0 turns off)
+  bool attn_tc = true;                   // tcgen05 attention for head_dim 64 (RV_ATTN_TC=0 turns off)
 
   std::vector<void*> allocations;
 

@@ -85,6 +85,20 @@ cudaError_t attention_varlen(Act act, const void* qkv, void* ctx, const int* cu_
                              int num_heads, int head_dim, int window_half, float scale,
                              cudaStream_t st);
 
+// The same on the 5th-generation tensor cores, head_dim 64 only.  tiles[t] = {sequence start,
+// length | first query << 16} of 128-query tile t (fill_attention_tiles); total_tokens bounds the
+// TMA view of qkv (total_tokens * heads * 64 < 2^31).  A pipeline wait that expires sets
+// kErrWaitTimeout in *err.
+cudaError_t attention_varlen_tc(Act act, const void* qkv, void* ctx, int total_tokens,
+                                const int2* tiles, int n_tiles, int num_heads, int window_half,
+                                float scale, unsigned int* err, cudaStream_t st);
+// Longest sequence the tile records encode.
+constexpr int kMaxAttnSeq = 32767;
+// Host: writes the 128-query tile records of a packed batch (sum of ceil(L_b / 128) entries,
+// at most total_tokens / 128 + n_seqs) and returns their count, or -1 when a length is negative
+// or above kMaxAttnSeq.
+int fill_attention_tiles(const int* cu_seqlens, int n_seqs, int2* out);
+
 // f32 -> 16-bit conversion (weights upload), n elements.
 cudaError_t convert_f32(Act act, const float* in, void* out, int64_t n, cudaStream_t st);
 

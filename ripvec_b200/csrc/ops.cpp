@@ -1,6 +1,8 @@
 // Single-kernel C entry points used by the parity tests (one kernel per call, device buffers).
 #include <cuda_runtime.h>
 
+#include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -78,30 +80,47 @@ int rv_op_attention(int32_t act_dtype, const void* qkv, void* ctx_out, const int
                     float scale, void* stream) {
   if (act_dtype != RV_DTYPE_BF16 && act_dtype != RV_DTYPE_F16) return RV_E_INVALID;
   if (n_seqs <= 0 || !cu_host || (head_dim != 64 && head_dim != 32)) return RV_E_INVALID;
-  std::vector<int> meta(2 * (n_seqs + 1));
+  for (int i = 0; i < n_seqs; ++i)
+    if (cu_host[i + 1] < cu_host[i]) return RV_E_INVALID;
+  const int total_tokens = cu_host[n_seqs];
+  // head_dim 64 runs on the tcgen05 kernel unless RV_ATTN_TC=0.
+  const char* env = std::getenv("RV_ATTN_TC");
+  const bool tc = head_dim == 64 && !(env && std::strcmp(env, "0") == 0) &&
+                  int64_t(total_tokens) * num_heads * head_dim <= INT32_MAX;
+  std::vector<int> meta;  // tc: int2 tile records; else cu_seqlens then 64-query tile starts
   int q = 0;
-  for (int i = 0; i <= n_seqs; ++i) {
-    meta[i] = cu_host[i];
-    meta[n_seqs + 1 + i] = q;
-    if (i < n_seqs) {
-      const int len = cu_host[i + 1] - cu_host[i];
-      if (len < 0) return RV_E_INVALID;
-      q += (len + 63) / 64;
+  if (tc) {
+    meta.resize(2 * (size_t(total_tokens) / 128 + n_seqs + 1));
+    q = rv::fill_attention_tiles(cu_host, n_seqs, reinterpret_cast<int2*>(meta.data()));
+    if (q < 0) return RV_E_INVALID;
+  } else {
+    meta.resize(2 * (n_seqs + 1));
+    for (int i = 0; i <= n_seqs; ++i) {
+      meta[i] = cu_host[i];
+      meta[n_seqs + 1 + i] = q;
+      if (i < n_seqs) q += (cu_host[i + 1] - cu_host[i] + 63) / 64;
     }
   }
+  unsigned int* err = op_err_word();
+  if (!err) return RV_E_CUDA;
   int* d = nullptr;
   if (cudaMalloc(&d, meta.size() * 4) != cudaSuccess) return RV_E_NOMEM;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const rv::Act act = act_dtype == RV_DTYPE_BF16 ? rv::Act::kBf16 : rv::Act::kF16;
   int rc = RV_OK;
   if (cudaMemcpyAsync(d, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
     rc = RV_E_CUDA;
-  if (rc == RV_OK &&
-      rv::attention_varlen(act_dtype == RV_DTYPE_BF16 ? rv::Act::kBf16 : rv::Act::kF16, qkv,
-                           ctx_out, d, d + n_seqs + 1, n_seqs, q, num_heads, head_dim, window_half,
-                           scale, st) != cudaSuccess)
-    rc = RV_E_CUDA;
+  if (rc == RV_OK) {
+    const cudaError_t e =
+        tc ? rv::attention_varlen_tc(act, qkv, ctx_out, total_tokens, reinterpret_cast<const int2*>(d), q,
+                                     num_heads, window_half, scale, err, st)
+           : rv::attention_varlen(act, qkv, ctx_out, d, d + n_seqs + 1, n_seqs, q, num_heads,
+                                  head_dim, window_half, scale, st);
+    if (e != cudaSuccess) rc = RV_E_CUDA;
+  }
   if (cudaStreamSynchronize(st) != cudaSuccess) rc = RV_E_CUDA;
   cudaFree(d);
+  if (rc == RV_OK) rc = check_err_word(err, st);
   return rc;
 }
 

@@ -70,11 +70,18 @@ def _attention_ref(qkv: np.ndarray, cu, heads, hd, window_half):
     return out
 
 
+@pytest.mark.parametrize("impl", ["tc", "mma"])
 @pytest.mark.parametrize("act", ["bf16", "f16"])
 @pytest.mark.parametrize("hd,heads,window", [(64, 12, -1), (64, 12, 64), (32, 12, -1), (64, 4, 64)])
-def test_attention_matches_oracle(cuda_device, act, hd, heads, window):
+def test_attention_matches_oracle(cuda_device, monkeypatch, impl, act, hd, heads, window):
+    """head_dim 64 runs the tcgen05 kernel ("tc") or, with RV_ATTN_TC=0, the mma.sync kernel;
+    head_dim 32 has only the mma.sync kernel."""
     torch = _torch()
     from ripvec_b200 import _lib as L
+
+    if impl == "tc" and hd != 64:
+        pytest.skip("the tcgen05 kernel covers head_dim 64")
+    monkeypatch.setenv("RV_ATTN_TC", "1" if impl == "tc" else "0")
 
     lengths = [1, 17, 63, 64, 65, 129, 300, 512, 0, 700]
     cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
@@ -91,6 +98,34 @@ def test_attention_matches_oracle(cuda_device, act, hd, heads, window):
     got = ctx.float().cpu().numpy()
     err = np.abs(got - ref).max()
     assert err < (3e-2 if act == "bf16" else 5e-3), err
+
+
+@pytest.mark.parametrize("window", [-1, 64])
+def test_attention_many_items_per_cta(cuda_device, monkeypatch, window):
+    """Enough 128-query tiles that every persistent CTA of the tcgen05 kernel walks dozens of
+    items, so Q, K/V and TMEM buffers rotate across item boundaries; ragged, empty and
+    one-token sequences interleaved."""
+    torch = _torch()
+    from ripvec_b200 import _lib as L
+
+    monkeypatch.setenv("RV_ATTN_TC", "1")
+    heads, hd = 12, 64
+    rng = np.random.default_rng(7 + window)
+    lengths = rng.integers(64, 513, size=400)
+    lengths[::37] = 0
+    lengths[5::41] = 1
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    T = int(cu[-1])
+    qkv = torch.from_numpy(rng.standard_normal((T, 3 * heads * hd)).astype(np.float32)).to(torch.bfloat16).cuda()
+    ctx = torch.full((T, heads * hd), float("nan"), device="cuda", dtype=torch.bfloat16)
+    rc = L.lib().rv_op_attention(L.RV_DTYPE_BF16, qkv.data_ptr(), ctx.data_ptr(), cu.ctypes.data, len(lengths),
+                                 heads, hd, window, float(1.0 / np.sqrt(hd)), _stream())
+    assert rc == 0
+    ref = _attention_ref(qkv.float().cpu().numpy(), cu, heads, hd, window)
+    got = ctx.float().cpu().numpy()
+    assert np.isfinite(got).all(), "rows left unwritten"
+    err = np.abs(got - ref).max()
+    assert err < 3e-2, err
 
 
 @pytest.mark.parametrize("hidden", [768, 384, 256])
