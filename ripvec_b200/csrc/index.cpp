@@ -3,7 +3,9 @@
 // index.rs:172-186, restricted to the best k with the (score desc, row asc) order).
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -44,8 +46,16 @@ struct Dev {
 };
 
 // Runs one query batch end to end on x->stream for candidate width kp.
+// Rows scored by the chunked path before the fused filter takes over (its lists give the
+// first thresholds).
+constexpr int64_t kFilterPrefixRows = 65536;
+
+// Runs one query batch end to end on x->stream for candidate width kp.  With `fused`, rows past
+// the first kFilterPrefixRows go through the filtering GEMM (scan_fused.cu) in blocks that grow
+// with the rows already seen; *x->overflow is set if a block kept more candidates than the
+// buffers hold, and the caller then redoes the batch without it.
 int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int k, int kp, float threshold,
-              int64_t* out_i, float* out_s, double* out_s64) {
+              int64_t* out_i, float* out_s, double* out_s64, bool fused) {
   cudaStream_t st = x->stream;
   if (!x->list_s.reserve(size_t(nq) * kp) || !x->list_i.reserve(size_t(nq) * kp) ||
       !x->list_n.reserve(size_t(nq)))
@@ -67,8 +77,9 @@ int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int k, int kp, float
       return ifail(x, RV_E_NOMEM, "scan score buffer allocation failed");
     int64_t r0 = 0;
     int64_t chunk = std::max<int64_t>(256, (cap - kp) / 256 * 256);
-    while (r0 < x->n) {
-      const int64_t valid = std::min<int64_t>(chunk, x->n - r0);
+    const int64_t chunked_end = fused ? std::min<int64_t>(x->n, kFilterPrefixRows) : x->n;
+    while (r0 < chunked_end) {
+      const int64_t valid = std::min<int64_t>(chunk, chunked_end - r0);
       const int64_t ncols = (valid + 255) / 256 * 256;
       rv::GemmArgs g{};
       g.tmA = &tq;
@@ -88,6 +99,34 @@ int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int k, int kp, float
       r0 += valid;
       const int64_t grow_to = (int64_t(cap - kp) * r0) / (4 * int64_t(kp));
       chunk = std::max<int64_t>(256, std::min<int64_t>(cmax, grow_to) / 256 * 256);
+    }
+    if (r0 < x->n) {
+      // Fused filter over the rest.  A block of b rows after s rows seen keeps about kp * b / s
+      // candidates per query on rows in random order; blocks of (cap / (2 kp)) * s rows keep that
+      // near half the buffer.
+      const int fcap = rv::scan_filter_cap();
+      const int nq_pad = (nq + 255) / 256 * 256;
+      if (!x->thr.reserve(size_t(nq_pad)) || !x->cand_n.reserve(size_t(nq)) ||
+          !x->cand_s.reserve(size_t(nq) * fcap) || !x->cand_i.reserve(size_t(nq) * fcap))
+        return ifail(x, RV_E_NOMEM, "scan filter buffer allocation failed");
+      CUtensorMap tq256;  // B operand: 256 query rows per tile
+      if (!rv::make_tmap_2d_16bit(&tq256, qb, true, x->dim, nq, uint64_t(x->dim) * 2, 64, 256, &why))
+        return ifail(x, RV_E_CUDA, why);
+      const int64_t grow = std::max<int64_t>(1, fcap / (2 * kp));
+      while (r0 < x->n) {
+        const int64_t rows = std::min<int64_t>({x->n - r0, std::max<int64_t>(262144, grow * r0),
+                                                int64_t(1) << 24});
+        CUtensorMap trows;
+        if (!rv::make_tmap_2d_16bit(&trows, x->db + size_t(r0) * x->dim, true, x->dim, uint64_t(rows),
+                                    uint64_t(x->dim) * 2, 64, 128, &why))
+          return ifail(x, RV_E_CUDA, why);
+        IX_TRY(x, rv::scan_filter_block(trows, tq256, static_cast<int>(rows), x->dim, x->base + r0, nq,
+                                        nq_pad, kp, x->thr.p, x->cand_n.p, x->cand_s.p, x->cand_i.p,
+                                        x->list_s.p, x->list_i.p, x->list_n.p, x->overflow.p, x->d_err,
+                                        st));
+        x->launches += 3;
+        r0 += rows;
+      }
     }
   }
   if (!x->cnt.reserve(size_t(nq)) || !x->guard.reserve(size_t(nq)))
@@ -109,13 +148,20 @@ int topk_device(rv_index* x, const float* q_dev, int nq, int k, float threshold,
   IX_TRY(x, rv::scan_round_queries(q_dev, x->qb.p, int64_t(nq) * x->dim, st));
   x->launches++;
   int kp = std::max(128, 2 * k);
+  // The fused filter needs the thresholds of all queries in shared memory (nq <= 2560).
+  bool fused = nq <= 2560 && !x->filter_off;
+  if (!x->overflow.reserve(1)) return ifail(x, RV_E_NOMEM, "scan flag allocation failed");
   for (;;) {
-    int rc = topk_pass(x, x->qb.p, nq, k, kp, threshold, out_i, out_s, out_s64);
+    const bool use_fused = fused && kp <= rv::scan_filter_max_kp();
+    IX_TRY(x, cudaMemsetAsync(x->overflow.p, 0, sizeof(int), st));
+    int rc = topk_pass(x, x->qb.p, nq, k, kp, threshold, out_i, out_s, out_s64, use_fused);
     if (rc) return rc;
     std::vector<int> g(nq);
     unsigned int e = 0;
+    int ovf = 0;
     IX_TRY(x, cudaMemcpyAsync(g.data(), x->guard.p, sizeof(int) * nq, cudaMemcpyDeviceToHost, st));
     IX_TRY(x, cudaMemcpyAsync(&e, x->d_err, 4, cudaMemcpyDeviceToHost, st));
+    IX_TRY(x, cudaMemcpyAsync(&ovf, x->overflow.p, sizeof(int), cudaMemcpyDeviceToHost, st));
     if (counts) {
       counts->resize(nq);
       IX_TRY(x, cudaMemcpyAsync(counts->data(), x->cnt.p, sizeof(int) * nq, cudaMemcpyDeviceToHost, st));
@@ -124,6 +170,11 @@ int topk_device(rv_index* x, const float* q_dev, int nq, int k, float threshold,
     if (e) {
       cudaMemset(x->d_err, 0, 4);
       return ifail(x, RV_E_DEVICE, "scan kernel reported device error flags " + std::to_string(e));
+    }
+    if (ovf) {
+      // A query kept more filter candidates than its buffer: same kp, chunked path only.
+      fused = false;
+      continue;
     }
     bool any = false;
     for (int v : g) any |= (v != 0);
@@ -151,6 +202,8 @@ int rv_index_create(int device, const void* src, int64_t n, int32_t dim, int32_t
   x->device = device;
   x->n = n;
   x->dim = dim;
+  // RV_SCAN_FILTER=0: score every row through the chunked GEMM + select path.
+  if (const char* e = std::getenv("RV_SCAN_FILTER")) x->filter_off = std::strcmp(e, "0") == 0;
   auto bail = [&](int code) {
     rv_index_destroy(x);
     return code;

@@ -47,6 +47,11 @@ struct rv_index {
   DevBuf<int64_t> list_i, oi;
   DevBuf<int> list_n, cnt, guard;
   DevBuf<double> os64;
+  // fused filter (scan_fused.cu): thresholds, candidate buffers, overflow flag
+  DevBuf<float> thr, cand_s;
+  DevBuf<int64_t> cand_i;
+  DevBuf<int> cand_n, overflow;
   int64_t launches = 0;
+  bool filter_off = false;  // RV_SCAN_FILTER=0 at creation
 };
 

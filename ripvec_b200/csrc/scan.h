@@ -1,6 +1,7 @@
 // Launchers of the exact top-k scan kernels (scan.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -22,5 +23,19 @@ cudaError_t scan_rescore(const __nv_bfloat16* db, int64_t base, int dim, const _
 cudaError_t scan_merge(const int64_t* idx_in, const double* s_in, int n_lists, int nq, int k,
                        float threshold, int64_t* idx_out, float* s_out, double* s64_out,
                        cudaStream_t st);
+
+// Fused filter (scan_fused.cu).  Candidate buffer size per query, largest list width.
+int scan_filter_cap();
+int scan_filter_max_kp();
+// Scores database rows [row0, row0 + rows) (tm_rows: their [rows, dim] bf16 view, box 64 x 128)
+// against the queries (tm_queries: [nq, dim] bf16, box 64 x 256, read as nq_pad rows, nq_pad a
+// multiple of 256 and <= 2560), keeps scores above each query's current kp-th list score, and
+// merges them into the lists.  thr: [nq_pad]; cand_*: [nq, scan_filter_cap()].  *overflow is set
+// when a query kept more candidates than the buffer holds (its list is then incomplete).
+cudaError_t scan_filter_block(const CUtensorMap& tm_rows, const CUtensorMap& tm_queries, int rows,
+                              int dim, int64_t row0, int nq, int nq_pad, int kp, float* thr,
+                              int* cand_n, float* cand_s, int64_t* cand_i, float* list_s,
+                              int64_t* list_i, int* list_n, int* overflow, unsigned int* err,
+                              cudaStream_t st);
 
 }  // namespace rv

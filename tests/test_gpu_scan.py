@@ -38,6 +38,46 @@ def test_topk_bit_exact_vs_oracle(cuda_device, n, dim, nq, k):
     np.testing.assert_array_equal(cnt, ec)
 
 
+def test_fused_filter_many_queries_bit_exact(cuda_device):
+    """Rows past the 65536-row prefix go through the filtering GEMM in growing blocks; 300 queries
+    pad to 512 GEMM columns.  Result bit-exact against the oracle."""
+    n, dim, nq, k = 200_000, 128, 300, 50
+    db = synth.normalized_gaussian(n, dim, seed=11)
+    q = synth.normalized_gaussian(nq, dim, seed=12)
+    ei, es, ec = scan.topk_exact(db, q, k)
+    oi, os_, cnt, o64 = SearchIndex(db).topk(q, k, with_f64=True)
+    np.testing.assert_array_equal(oi, ei)
+    np.testing.assert_array_equal(o64, es)
+    np.testing.assert_array_equal(cnt, ec)
+
+
+def test_fused_filter_overflow_falls_back(cuda_device):
+    """Every row after the prefix is a near copy of the query, so each filter block keeps far more
+    candidates than its buffer: the batch is redone on the chunked path and stays exact."""
+    n, dim = 150_000, 128
+    db = synth.normalized_gaussian(n, dim, seed=13)
+    rng = np.random.default_rng(14)
+    tail = db[0] + 0.01 * rng.standard_normal((n - 70_000, dim)).astype(np.float32)
+    db[70_000:] = tail / np.linalg.norm(tail, axis=1, keepdims=True)
+    q = db[0:2].copy()
+    ei, es, ec = scan.topk_exact(db, q, 100)
+    oi, os_, cnt, o64 = SearchIndex(db).topk(q, 100, with_f64=True)
+    np.testing.assert_array_equal(oi, ei)
+    np.testing.assert_array_equal(o64, es)
+
+
+def test_fused_filter_matches_chunked_path(cuda_device, monkeypatch):
+    """The same index answered with the filter and with RV_SCAN_FILTER=0 (every row through the
+    chunked GEMM + select) gives identical indices and f64 scores."""
+    db = synth.normalized_gaussian(300_000, 384, seed=15)
+    q = synth.normalized_gaussian(64, 384, seed=16)
+    a = SearchIndex(db).topk(q, 100, with_f64=True)
+    monkeypatch.setenv("RV_SCAN_FILTER", "0")
+    b = SearchIndex(db).topk(q, 100, with_f64=True)
+    for x, y in zip(a, b):
+        np.testing.assert_array_equal(x, y)
+
+
 def test_threshold_k_larger_than_n_and_empty_index(cuda_device):
     db = synth.normalized_gaussian(300, 64, seed=3)
     q = synth.normalized_gaussian(2, 64, seed=4)
