@@ -114,32 +114,6 @@ __device__ __forceinline__ int half_class(int kb, int L, int qa, int qb, int wh)
   return (ke < L && kb >= qb - wh && ke <= qa + wh) ? 2 : 1;
 }
 
-// Packed f32x2 arithmetic (one instruction for two lanes of a 64-bit register pair) and the
-// three-input max of sm_100.
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
 // Masks (class 1) the 32 scores of keys kb..kb+31 for query qi to -inf and returns their max.
 __device__ __forceinline__ float masked_max(float (&s)[32], int cls, int kb, int L, int qi, int wh) {
   if (cls == 1) {

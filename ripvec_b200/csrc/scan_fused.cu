@@ -34,12 +34,12 @@ struct EpiTopKFilter {
   int cap;
   int n_thr;     // staged thresholds: nq_pad (queries past nq have +inf)
   int64_t row0;  // global index of block row 0
-  const float* thr_s = nullptr;
+  const float* nthr_s = nullptr;  // staged -thr
   using Pre = NoPre;
   using Tile = NoTile;
   __device__ __forceinline__ void stage(float* s, int t, int nt) {
-    for (int i = t; i < n_thr; i += nt) s[i] = thr[i];
-    thr_s = s;
+    for (int i = t; i < n_thr; i += nt) s[i] = -thr[i];
+    nthr_s = s;
   }
   __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
   __device__ __forceinline__ void load(Pre&, int, int) const {}
@@ -50,21 +50,31 @@ struct EpiTopKFilter {
       cand_i[static_cast<size_t>(q) * cap + p] = row0 + row;
     }
   }
-  __device__ __forceinline__ void apply(const Pre&, Tile&, int row, int col, const float (&v0)[32],
-                                        const float (&v1)[32]) const {
-    const float4* t4 = reinterpret_cast<const float4*>(thr_s + col);
-    // Queries past nq have threshold +inf in the staged copy (see scan_filter_block).
+  // max over 32 columns of v - thr (packed adds of -thr, three-input maxima): > 0 iff a score of
+  // the 32 passes (v - thr of finite floats is exact in sign; -inf / +inf thresholds give +inf /
+  // -inf).
+  __device__ __forceinline__ float margin32(const float (&v)[32], const float4* nt) const {
+    float mx = -INFINITY;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float4 a = t4[i], b = t4[8 + i];
-      if (v0[4 * i] > a.x) keep(col + 4 * i, v0[4 * i], row);
-      if (v0[4 * i + 1] > a.y) keep(col + 4 * i + 1, v0[4 * i + 1], row);
-      if (v0[4 * i + 2] > a.z) keep(col + 4 * i + 2, v0[4 * i + 2], row);
-      if (v0[4 * i + 3] > a.w) keep(col + 4 * i + 3, v0[4 * i + 3], row);
-      if (v1[4 * i] > b.x) keep(col + 32 + 4 * i, v1[4 * i], row);
-      if (v1[4 * i + 1] > b.y) keep(col + 32 + 4 * i + 1, v1[4 * i + 1], row);
-      if (v1[4 * i + 2] > b.z) keep(col + 32 + 4 * i + 2, v1[4 * i + 2], row);
-      if (v1[4 * i + 3] > b.w) keep(col + 32 + 4 * i + 3, v1[4 * i + 3], row);
+      const float4 a = nt[i];
+      float d0, d1, d2, d3;
+      f2_unpack(f2_add(f2_pack(v[4 * i], v[4 * i + 1]), f2_pack(a.x, a.y)), d0, d1);
+      f2_unpack(f2_add(f2_pack(v[4 * i + 2], v[4 * i + 3]), f2_pack(a.z, a.w)), d2, d3);
+      mx = fmax3(mx, fmaxf(d0, d1), fmaxf(d2, d3));
+    }
+    return mx;
+  }
+  __device__ __forceinline__ void apply(const Pre&, Tile&, int row, int col, const float (&v0)[32],
+                                        const float (&v1)[32]) const {
+    // Queries past nq have threshold +inf in the staged copy (see scan_filter_block).
+    const float4* nt = reinterpret_cast<const float4*>(nthr_s + col);
+    if (fmaxf(margin32(v0, nt), margin32(v1, nt + 8)) > 0.f) {  // rare: some score passes
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (v0[i] > -nthr_s[col + i]) keep(col + i, v0[i], row);
+        if (v1[i] > -nthr_s[col + 32 + i]) keep(col + 32 + i, v1[i], row);
+      }
     }
   }
 };
