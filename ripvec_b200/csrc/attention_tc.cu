@@ -430,10 +430,12 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         const int qa = wk.q0 + quad * 32;
         const int kb = (wk.t_lo + wk.j) * kBKV + 32 * half;
         cls = half_class(kb, wk.L, qa, qa + 31, window_half);
-        // Every warp waits for every tile's scores, so the phases it tracks never fall behind.
+        // Every warp waits for every tile's scores.  S of tile g is committed after the MMA thread
+        // issued P V of tile g - 2 and tcgen05.commit tracks every earlier MMA of that thread, so
+        // this wait also means: P slot b is free, and P V of g - 2 (so of g - 3 as well) has
+        // updated O.  The rescale and read-out waits on p_empty below therefore always target
+        // the barrier's current phase.
         fail = fail || !__all_sync(0xffffffffu, mbar_wait(&s_full[b], ph, abort_flag));
-        // P slot b is free once the P V MMA of tile g - 2 completed (almost always already true).
-        fail = fail || !__all_sync(0xffffffffu, mbar_wait(&p_empty[b], ph ^ 1u, abort_flag));
         float mt = -INFINITY;
         if (!fail && cls) {
           tc_fence_after();

@@ -15,6 +15,9 @@
 // :519-543), which become epilogues of the one kernel.
 #pragma once
 
+#include <type_traits>
+#include <utility>
+
 #include "common.cuh"
 
 namespace rv {
@@ -43,6 +46,13 @@ struct GemmCfg {
 
 struct NoPre {};
 struct NoTile {};
+
+// Optional epilogue hook `finish(int t)`, called once by each of the 128 epilogue threads (index
+// t) after the CTA's last tile, behind a barrier of those threads.
+template <class E, class = void>
+struct HasFinish : std::false_type {};
+template <class E>
+struct HasFinish<E, std::void_t<decltype(std::declval<const E&>().finish(0))>> : std::true_type {};
 
 template <typename T>
 struct EpiStore {
@@ -411,6 +421,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (!ok && lane == 0) {
       *abort_flag = 1;
       atomicOr(err, kErrWaitTimeout);
+    }
+    if constexpr (HasFinish<Epi>::value) {
+      // Every epilogue warp reaches this point exactly once (finished or aborted), so the
+      // barrier of the 128 epilogue threads always completes.
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      epi.finish(threadIdx.x - 64);
     }
   }
 

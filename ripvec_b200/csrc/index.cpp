@@ -102,26 +102,29 @@ int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int k, int kp, float
     }
     if (r0 < x->n) {
       // Fused filter over the rest.  A block of b rows after s rows seen keeps about kp * b / s
-      // candidates per query on rows in random order; blocks of (cap / (2 kp)) * s rows keep that
-      // near half the buffer.
+      // candidates per query on rows in random order; blocks of s rows keep about kp each, and
+      // the total over the ln(n / s0) / ln 2 blocks, 1.45 kp ln(n / s0), is about half of what
+      // fewer, larger blocks keep.
       const int fcap = rv::scan_filter_cap();
       const int nq_pad = (nq + 255) / 256 * 256;
+      const int sms = rv::device_sm_count();
       if (!x->thr.reserve(size_t(nq_pad)) || !x->cand_n.reserve(size_t(nq)) ||
-          !x->cand_s.reserve(size_t(nq) * fcap) || !x->cand_i.reserve(size_t(nq) * fcap))
+          !x->cand_s.reserve(size_t(nq) * fcap) || !x->cand_i.reserve(size_t(nq) * fcap) ||
+          !x->rec_n.reserve(size_t(sms)) ||
+          !x->rec.reserve(size_t(sms) * size_t(rv::scan_filter_record_cap())))
         return ifail(x, RV_E_NOMEM, "scan filter buffer allocation failed");
       CUtensorMap tq256;  // B operand: 256 query rows per tile
       if (!rv::make_tmap_2d_16bit(&tq256, qb, true, x->dim, nq, uint64_t(x->dim) * 2, 64, 256, &why))
         return ifail(x, RV_E_CUDA, why);
-      const int64_t grow = std::max<int64_t>(1, fcap / (2 * kp));
       while (r0 < x->n) {
-        const int64_t rows = std::min<int64_t>({x->n - r0, std::max<int64_t>(262144, grow * r0),
-                                                int64_t(1) << 24});
+        const int64_t rows = std::min<int64_t>({x->n - r0, std::max<int64_t>(65536, r0), int64_t(1) << 24});
         CUtensorMap trows;
         if (!rv::make_tmap_2d_16bit(&trows, x->db + size_t(r0) * x->dim, true, x->dim, uint64_t(rows),
                                     uint64_t(x->dim) * 2, 64, 128, &why))
           return ifail(x, RV_E_CUDA, why);
         IX_TRY(x, rv::scan_filter_block(trows, tq256, static_cast<int>(rows), x->dim, x->base + r0, nq,
-                                        nq_pad, kp, x->thr.p, x->cand_n.p, x->cand_s.p, x->cand_i.p,
+                                        nq_pad, kp, x->thr.p, x->rec.p, x->rec_n.p, x->cand_n.p,
+                                        x->cand_s.p, x->cand_i.p,
                                         x->list_s.p, x->list_i.p, x->list_n.p, x->overflow.p, x->d_err,
                                         st));
         x->launches += 3;
@@ -148,8 +151,8 @@ int topk_device(rv_index* x, const float* q_dev, int nq, int k, float threshold,
   IX_TRY(x, rv::scan_round_queries(q_dev, x->qb.p, int64_t(nq) * x->dim, st));
   x->launches++;
   int kp = std::max(128, 2 * k);
-  // The fused filter needs the thresholds of all queries in shared memory (nq <= 2560).
-  bool fused = nq <= 2560 && !x->filter_off;
+  // The fused filter needs the thresholds of all queries in shared memory.
+  bool fused = nq <= rv::scan_filter_max_queries() && !x->filter_off;
   if (!x->overflow.reserve(1)) return ifail(x, RV_E_NOMEM, "scan flag allocation failed");
   for (;;) {
     const bool use_fused = fused && kp <= rv::scan_filter_max_kp();

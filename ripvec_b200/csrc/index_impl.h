@@ -50,7 +50,8 @@ struct rv_index {
   // fused filter (scan_fused.cu): thresholds, candidate buffers, overflow flag
   DevBuf<float> thr, cand_s;
   DevBuf<int64_t> cand_i;
-  DevBuf<int> cand_n, overflow;
+  DevBuf<int> cand_n, overflow, rec_n;
+  DevBuf<int4> rec;
   int64_t launches = 0;
   bool filter_off = false;  // RV_SCAN_FILTER=0 at creation
 };

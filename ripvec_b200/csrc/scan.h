@@ -24,18 +24,22 @@ cudaError_t scan_merge(const int64_t* idx_in, const double* s_in, int n_lists, i
                        float threshold, int64_t* idx_out, float* s_out, double* s64_out,
                        cudaStream_t st);
 
-// Fused filter (scan_fused.cu).  Candidate buffer size per query, largest list width.
+// Fused filter (scan_fused.cu).  Candidate buffer size per query, largest list width, most
+// queries per batch, records per GEMM CTA.
 int scan_filter_cap();
 int scan_filter_max_kp();
+int scan_filter_max_queries();
+int scan_filter_record_cap();
 // Scores database rows [row0, row0 + rows) (tm_rows: their [rows, dim] bf16 view, box 64 x 128)
 // against the queries (tm_queries: [nq, dim] bf16, box 64 x 256, read as nq_pad rows, nq_pad a
-// multiple of 256 and <= 2560), keeps scores above each query's current kp-th list score, and
-// merges them into the lists.  thr: [nq_pad]; cand_*: [nq, scan_filter_cap()].  *overflow is set
-// when a query kept more candidates than the buffer holds (its list is then incomplete).
+// multiple of 256 and <= scan_filter_max_queries()), keeps scores above each query's current
+// kp-th list score, and merges them into the lists.  thr: [nq_pad]; rec: [sms, record cap];
+// rec_n: [sms]; cand_*: [nq, scan_filter_cap()].  *overflow is set when a CTA or a query kept
+// more candidates than its buffer holds (the lists are then incomplete).
 cudaError_t scan_filter_block(const CUtensorMap& tm_rows, const CUtensorMap& tm_queries, int rows,
                               int dim, int64_t row0, int nq, int nq_pad, int kp, float* thr,
-                              int* cand_n, float* cand_s, int64_t* cand_i, float* list_s,
-                              int64_t* list_i, int* list_n, int* overflow, unsigned int* err,
-                              cudaStream_t st);
+                              int4* rec, int* rec_n, int* cand_n, float* cand_s, int64_t* cand_i,
+                              float* list_s, int64_t* list_i, int* list_n, int* overflow,
+                              unsigned int* err, cudaStream_t st);
 
 }  // namespace rv

@@ -23,32 +23,38 @@ namespace {
 
 constexpr int kFilterMaxKp = 512;  // larger candidate lists use the chunked path only
 
-// Epilogue of the filtering GEMM: row = database row of the block, col = query.  The thresholds
-// of all queries are staged in shared memory.  The count keeps growing past cap, so an overflow
-// is visible to the merge.
+constexpr int kFilterMaxThr = 2048;  // staged thresholds (queries); the CTA's counter follows
+
+// Epilogue of the filtering GEMM: row = database row of the block, col = query.  The negated
+// thresholds of all queries and the CTA's record counter live in the staging shared memory.  A
+// kept score becomes a {query, block row, score bits} record in the CTA's own region of `rec`;
+// the slot comes from the shared counter, so keeping costs a shared atomic and a plain store
+// instead of a global atomic round trip per candidate.  finish() publishes the count (which may
+// exceed rec_cap: the bucket kernel then reports an overflow).
 struct EpiTopKFilter {
-  const float* thr;  // [nq]
-  int* cand_n;       // [nq]
-  float* cand_s;     // [nq, cap]
-  int64_t* cand_i;   // [nq, cap]
-  int cap;
-  int n_thr;     // staged thresholds: nq_pad (queries past nq have +inf)
-  int64_t row0;  // global index of block row 0
+  const float* thr;  // [n_thr]
+  int4* rec;         // [grid][rec_cap]
+  int* rec_n;        // [grid]
+  int rec_cap;
+  int n_thr;         // staged thresholds: nq_pad (queries past nq have +inf)
   const float* nthr_s = nullptr;  // staged -thr
+  int* cnt_s = nullptr;
   using Pre = NoPre;
   using Tile = NoTile;
   __device__ __forceinline__ void stage(float* s, int t, int nt) {
     for (int i = t; i < n_thr; i += nt) s[i] = -thr[i];
     nthr_s = s;
+    cnt_s = reinterpret_cast<int*>(s + kFilterMaxThr);
+    if (t == 0) *cnt_s = 0;
   }
   __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
   __device__ __forceinline__ void load(Pre&, int, int) const {}
-  __device__ __forceinline__ void keep(int q, float v, int row) const {
-    const int p = atomicAdd(&cand_n[q], 1);
-    if (p < cap) {
-      cand_s[static_cast<size_t>(q) * cap + p] = v;
-      cand_i[static_cast<size_t>(q) * cap + p] = row0 + row;
-    }
+  __device__ __forceinline__ void put(int p, int q, float v, int row) const {
+    if (p < rec_cap)
+      rec[static_cast<size_t>(blockIdx.x) * rec_cap + p] = make_int4(q, row, __float_as_int(v), 0);
+  }
+  __device__ __forceinline__ void finish(int t) const {
+    if (t == 0) rec_n[blockIdx.x] = *cnt_s;
   }
   // max over 32 columns of v - thr (packed adds of -thr, three-input maxima): > 0 iff a score of
   // the 32 passes (v - thr of finite floats is exact in sign; -inf / +inf thresholds give +inf /
@@ -65,19 +71,60 @@ struct EpiTopKFilter {
     }
     return mx;
   }
+  // Called by the lanes whose row is inside the matrix (a prefix of the warp's lanes).
   __device__ __forceinline__ void apply(const Pre&, Tile&, int row, int col, const float (&v0)[32],
                                         const float (&v1)[32]) const {
-    // Queries past nq have threshold +inf in the staged copy (see scan_filter_block).
     const float4* nt = reinterpret_cast<const float4*>(nthr_s + col);
-    if (fmaxf(margin32(v0, nt), margin32(v1, nt + 8)) > 0.f) {  // rare: some score passes
+    const unsigned am = __activemask();
+    const bool hit = fmaxf(margin32(v0, nt), margin32(v1, nt + 8)) > 0.f;
+    if (!__any_sync(am, hit)) return;  // common case: nothing in these 64 columns passes
+    // Slots for the warp's records: per-lane counts, a warp prefix sum, one shared atomic.
+    int cnt = 0;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (v0[i] > -nthr_s[col + i]) keep(col + i, v0[i], row);
-        if (v1[i] > -nthr_s[col + 32 + i]) keep(col + 32 + i, v1[i], row);
-      }
+    for (int i = 0; i < 32; ++i)
+      cnt += (v0[i] > -nthr_s[col + i] ? 1 : 0) + (v1[i] > -nthr_s[col + 32 + i] ? 1 : 0);
+    const int lane = threadIdx.x & 31;
+    const int last = 31 - __clz(am);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(am, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int base = 0;
+    if (lane == last) base = atomicAdd(cnt_s, incl);
+    base = __shfl_sync(am, base, last);
+    if (cnt == 0) return;
+    int p = base + incl - cnt;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (v0[i] > -nthr_s[col + i]) put(p++, col + i, v0[i], row);
+      if (v1[i] > -nthr_s[col + 32 + i]) put(p++, col + 32 + i, v1[i], row);
     }
   }
 };
+
+// Block c moves the records of GEMM CTA c into the per-query candidate buffers (global row =
+// row0 + block row).  A CTA that kept more records than its region holds sets *overflow.
+__global__ void __launch_bounds__(256) filter_bucket_kernel(const int4* __restrict__ rec,
+                                                            const int* __restrict__ rec_n, int rec_cap,
+                                                            int64_t row0, int cap, int* __restrict__ cand_n,
+                                                            float* __restrict__ cand_s,
+                                                            int64_t* __restrict__ cand_i,
+                                                            int* __restrict__ overflow) {
+  const int c = blockIdx.x;
+  const int n = rec_n[c];
+  if (n > rec_cap && threadIdx.x == 0) atomicExch(overflow, 1);
+  const int m = min(n, rec_cap);
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    const int4 r = rec[static_cast<size_t>(c) * rec_cap + i];
+    const int p = atomicAdd(&cand_n[r.x], 1);
+    if (p < cap) {
+      cand_s[static_cast<size_t>(r.x) * cap + p] = __int_as_float(r.z);
+      cand_i[static_cast<size_t>(r.x) * cap + p] = row0 + r.y;
+    }
+  }
+}
 
 // thr[q] = the list's kp-th score (-inf while the list is short); +inf for padded queries
 // [nq, nq_pad) so that they never keep anything; cand_n = 0.
@@ -145,21 +192,30 @@ __global__ void __launch_bounds__(256) filter_merge_kernel(const float* __restri
 
 int scan_filter_cap() { return 2048; }
 int scan_filter_max_kp() { return kFilterMaxKp; }
+int scan_filter_max_queries() { return kFilterMaxThr; }
+int scan_filter_record_cap() { return 32768; }
 
 cudaError_t scan_filter_block(const CUtensorMap& tm_rows, const CUtensorMap& tm_queries, int rows,
                               int dim, int64_t row0, int nq, int nq_pad, int kp, float* thr,
-                              int* cand_n, float* cand_s, int64_t* cand_i, float* list_s,
-                              int64_t* list_i, int* list_n, int* overflow, unsigned int* err,
-                              cudaStream_t st) {
+                              int4* rec, int* rec_n, int* cand_n, float* cand_s, int64_t* cand_i,
+                              float* list_s, int64_t* list_i, int* list_n, int* overflow,
+                              unsigned int* err, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  if (nq_pad % 256 != 0 || nq_pad > 2560 || nq > nq_pad || dim % 64 != 0 || kp > kFilterMaxKp)
+  if (nq_pad % 256 != 0 || nq_pad > kFilterMaxThr || nq > nq_pad || dim % 64 != 0 || kp > kFilterMaxKp)
     return cudaErrorInvalidValue;
   const int cap = scan_filter_cap();
+  const int rec_cap = scan_filter_record_cap();
+  const int sms = device_sm_count();
   filter_prepare_kernel<<<(nq_pad + 255) / 256, 256, 0, st>>>(list_s, list_n, kp, nq, nq_pad, thr, cand_n);
-  EpiTopKFilter epi{thr, cand_n, cand_s, cand_i, cap, nq_pad, row0};
+  EpiTopKFilter epi{thr, rec, rec_n, rec_cap, nq_pad};
   cudaError_t e = launch_gemm_tc<__nv_bfloat16, 256>(tm_rows, tm_queries, rows, nq_pad, dim, 0, epi,
-                                                      err, device_sm_count(), st);
+                                                      err, sms, st);
   if (e != cudaSuccess) return e;
+  // The GEMM ran min(tiles, sms) persistent CTAs (launch_gemm_tc), each of which wrote rec_n.
+  const int64_t tiles = (int64_t(rows) + kGemmBM - 1) / kGemmBM * (nq_pad / 256);
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  filter_bucket_kernel<<<grid, 256, 0, st>>>(rec, rec_n, rec_cap, row0, cap, cand_n, cand_s, cand_i,
+                                             overflow);
   int n = 1;
   while (n < cap + kp) n <<= 1;
   const size_t smem = size_t(n) * (sizeof(int64_t) + sizeof(float));
