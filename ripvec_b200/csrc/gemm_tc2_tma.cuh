@@ -21,12 +21,15 @@ struct Gemm2TmaCfg {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;
   static constexpr int kBBytes = kHalfN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;  // 32 KB
-  static constexpr int kStages = 5;
-  static constexpr int kRing = 3;
+  static constexpr int kStages = 4;
+  static constexpr int kEpiGroups = 2;                    // epilogue warpgroups (one per accumulator)
+  static constexpr int kRing = 2;                         // staging tiles per epilogue warpgroup
   static constexpr int kRingBytes = 16384;                // 128 rows x 128 B
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kEpiSmemBytes = 10240;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kRing * kRingBytes + 256 + kEpiSmemBytes;
+  static constexpr int kThreads = 64 + 128 * kEpiGroups;  // producer, MMA issuer, 8 epilogue warps
+  static constexpr int kSmemBytes =
+      1024 + kStages * kStageBytes + kEpiGroups * kRing * kRingBytes + 256 + kEpiSmemBytes;
 };
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
@@ -44,18 +47,18 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-// Named barrier over the 128 epilogue threads that also returns the OR of `fail` over them, so
-// that every thread takes the same exit decision (no thread is ever left alone at a barrier).
-__device__ __forceinline__ bool epi_bar_any(bool fail) {
+// Named barrier `id` over the 128 threads of one epilogue warpgroup that also returns the OR of
+// `fail` over them, so that every thread takes the same exit decision (no thread is ever left
+// alone at a barrier).
+__device__ __forceinline__ bool epi_bar_any(int id, bool fail) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 128, p;\n\t"
+      "bar.red.or.pred q, %2, 128, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}\n"
       : "=r"(r)
-      : "r"(static_cast<uint32_t>(fail))
+      : "r"(static_cast<uint32_t>(fail)), "r"(id)
       : "memory");
   return r != 0;
 }
@@ -69,7 +72,7 @@ __device__ __forceinline__ uint32_t swz(int r, int j) {
 }
 
 template <typename T, class Epi>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2TmaCfg::kThreads, 1)
     gemm_tc2_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, int M, int N, int K, Epi epi,
                         unsigned int* err) {
@@ -86,15 +89,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * Cfg::kABytes;
   uint8_t* ring = smem + kStages * Cfg::kStageBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + Cfg::kRing * Cfg::kRingBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + Cfg::kEpiGroups * Cfg::kRing * Cfg::kRingBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* rfull = drain + 1;  // kRing
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + Cfg::kRing);
+  uint64_t* rfull = drain + 1;  // [kEpiGroups][kRing]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + Cfg::kEpiGroups * Cfg::kRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* epi_smem = reinterpret_cast<float*>(ring + Cfg::kRing * Cfg::kRingBytes + 256);
+  float* epi_smem = reinterpret_cast<float*>(ring + Cfg::kEpiGroups * Cfg::kRing * Cfg::kRingBytes + 256);
 
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -111,7 +114,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tempty[a], 8);
     }
     mbar_init(drain, 1);
-    for (int b = 0; b < Cfg::kRing; ++b) mbar_init(&rfull[b], 1);
+    for (int b = 0; b < Cfg::kEpiGroups * Cfg::kRing; ++b) mbar_init(&rfull[b], 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -195,45 +198,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait_cluster(drain, 0, &no_abort)) atomicOr(err, kErrWaitTimeout);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (128 threads)
+    // ---------------------------------------------------------------- epilogue (2 x 128 threads)
+    // Epilogue warpgroup ewg drains accumulator ewg, i.e. every other tile of the CTA, through
+    // its own staging ring, barriers and TMA-issuing thread; the two warpgroups work on
+    // consecutive tiles at the same time.
+    const int ewg = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int rl = quad * 32 + lane;             // row inside this CTA's 128-row block = TMEM lane
-    const bool e0 = threadIdx.x == 64;           // issues the ring's TMA loads and stores
+    const int bar_id = 1 + ewg;
+    const bool e0 = threadIdx.x == 64 + 128 * ewg;  // issues this warpgroup's TMA loads and stores
+    uint8_t* ring_e = ring + ewg * Cfg::kRing * Cfg::kRingBytes;
+    uint64_t* rfull_e = rfull + ewg * Cfg::kRing;
     const uint32_t tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
-    epi.stage(epi_smem, threadIdx.x - 64, 128);
-    epi_bar();
+    epi.stage(epi_smem, threadIdx.x - 64, 128 * Cfg::kEpiGroups);
+    asm volatile("bar.sync 3, %0;" ::"n"(128 * Cfg::kEpiGroups) : "memory");
     constexpr int kGroups = kBN / 64;
     const int my_tiles = cluster_id < num_tiles ? (num_tiles - 1 - cluster_id) / num_clusters + 1 : 0;
-    const int total_groups = my_tiles * kGroups;
-    // Coordinates of group q of this CTA: tile index and column.
-    auto group_tile = [&](int q) { return cluster_id + (q / kGroups) * num_clusters; };
+    const int ew_tiles = my_tiles > ewg ? (my_tiles - 1 - ewg) / Cfg::kEpiGroups + 1 : 0;
+    const int total_groups = ew_tiles * kGroups;
+    // Group q of this warpgroup: its (q / kGroups)-th tile, i.e. CTA tile it = 2 (q / kGroups) + ewg.
+    auto group_tile = [&](int q) { return cluster_id + (Cfg::kEpiGroups * (q / kGroups) + ewg) * num_clusters; };
     if (Epi::kReadsC && e0 && total_groups > 0) {
       const int t = group_tile(0);
-      mbar_arrive_expect_tx(&rfull[0], Cfg::kRingBytes);
-      tma_load_2d(ring, &tmC, &rfull[0], (t % num_n) * kBN, (t / num_n) * (2 * kGemmBM) + int(rank) * kGemmBM);
+      mbar_arrive_expect_tx(&rfull_e[0], Cfg::kRingBytes);
+      tma_load_2d(ring_e, &tmC, &rfull_e[0], (t % num_n) * kBN, (t / num_n) * (2 * kGemmBM) + int(rank) * kGemmBM);
     }
     bool ok = true;
     int last_load = Epi::kReadsC && total_groups > 0 ? 0 : -1;  // newest group whose C load is in flight
     typename Epi::Tile tile;
     for (int q = 0; q < total_groups; ++q) {
       const int g = q % kGroups;
-      const int it = q / kGroups;
+      const int j = q / kGroups;
       const int t = group_tile(q);
-      const int acc = it & 1;
-      const uint32_t acc_phase = (it >> 1) & 1;
+      const int acc = ewg;
+      const uint32_t acc_phase = j & 1;  // accumulator ewg's j-th use
       const int m0 = (t / num_n) * (2 * kGemmBM) + static_cast<int>(rank) * kGemmBM;
       const int n0 = (t % num_n) * kBN;
       const int row = m0 + rl;
       const bool live = row < M;
       const int b = q % Cfg::kRing;
-      uint8_t* buf = ring + b * Cfg::kRingBytes;
+      uint8_t* buf = ring_e + b * Cfg::kRingBytes;
       if (e0) {
-        bulk_wait_read<1>();  // the store that last used ring slot (q+1)%3 has read its tile
+        // The store that last used slot b (group q - kRing) has read its tile; when C is read, the
+        // slot of group q + 1 (that of q - 1 with two slots) must be free as well.
+        if (Epi::kReadsC) bulk_wait_read<0>();
+        else bulk_wait_read<Cfg::kRing - 1>();
         if (Epi::kReadsC && q + 1 < total_groups) {
           const int qn = q + 1, tn = group_tile(qn), bn = qn % Cfg::kRing;
           fence_proxy_async();
-          mbar_arrive_expect_tx(&rfull[bn], Cfg::kRingBytes);
-          tma_load_2d(ring + bn * Cfg::kRingBytes, &tmC, &rfull[bn], (tn % num_n) * kBN + (qn % kGroups) * 64,
+          mbar_arrive_expect_tx(&rfull_e[bn], Cfg::kRingBytes);
+          tma_load_2d(ring_e + bn * Cfg::kRingBytes, &tmC, &rfull_e[bn], (tn % num_n) * kBN + (qn % kGroups) * 64,
                       (tn / num_n) * (2 * kGemmBM) + int(rank) * kGemmBM);
           last_load = qn;
         }
@@ -260,24 +274,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       }
       float r[64];
       if (Epi::kReadsC && !fail) {
-        const bool w = mbar_wait(&rfull[b], (q / Cfg::kRing) & 1, abort_flag);
+        const bool w = mbar_wait(&rfull_e[b], (q / Cfg::kRing) & 1, abort_flag);
         fail = !__all_sync(0xffffffffu, w);
         if (!fail) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            unpack8<T>(*reinterpret_cast<const uint4*>(buf + swz<128>(rl, j)), &r[8 * j]);
+          for (int jj = 0; jj < 8; ++jj)
+            unpack8<T>(*reinterpret_cast<const uint4*>(buf + swz<128>(rl, jj)), &r[8 * jj]);
         }
       }
       if (!fail) {
         epi.compute(tile, row, n0 + g * 64, r, v0, v1, live);
 #pragma unroll
-        for (int j = 0; j < kOutCols / 8; ++j) {
-          const float* v = (j < 4) ? &v0[8 * j] : &v1[8 * (j - 4)];
-          *reinterpret_cast<uint4*>(buf + swz<kRowBytes>(rl, j)) = pack8<T>(v);
+        for (int jj = 0; jj < kOutCols / 8; ++jj) {
+          const float* v = (jj < 4) ? &v0[8 * jj] : &v1[8 * (jj - 4)];
+          *reinterpret_cast<uint4*>(buf + swz<kRowBytes>(rl, jj)) = pack8<T>(v);
         }
       }
       fence_proxy_async();
-      if (epi_bar_any(fail || *abort_flag != 0)) {
+      if (epi_bar_any(bar_id, fail || *abort_flag != 0)) {
         ok = false;
         break;
       }
@@ -289,7 +303,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
     if (!ok && e0 && last_load >= 0) {  // let the C load still in flight land (bounded)
       volatile int no_abort = 0;
-      mbar_wait(&rfull[last_load % Cfg::kRing], (last_load / Cfg::kRing) & 1, &no_abort);
+      mbar_wait(&rfull_e[last_load % Cfg::kRing], (last_load / Cfg::kRing) & 1, &no_abort);
     }
     if (!ok && lane == 0) {
       *abort_flag = 1;
@@ -323,8 +337,8 @@ cudaError_t launch_gemm_tc2_tma(const CUtensorMap& tmA, const CUtensorMap& tmB, 
   if (N % Cfg::kBN != 0 || K % kGemmBK != 0) return cudaErrorInvalidValue;
   const int tiles = ((M + 2 * kGemmBM - 1) / (2 * kGemmBM)) * (N / Cfg::kBN);
   const int clusters = tiles < num_sms / 2 ? tiles : num_sms / 2;
-  gemm_tc2_tma_kernel<T, Epi><<<2 * clusters, kGemmThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmC, M, N, K, epi,
-                                                                                      err);
+  gemm_tc2_tma_kernel<T, Epi><<<2 * clusters, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmC, M, N, K,
+                                                                                        epi, err);
   return cudaGetLastError();
 }
 
