@@ -49,6 +49,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Same, letting the thread sleep up to `ns` nanoseconds inside the instruction; it resumes as
+// soon as the phase completes, so a waiting warp stops taking issue slots from the warps that
+// share its scheduler.
+constexpr uint32_t kSuspendHintNs = 2000;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
 // Waits for the phase with the given parity to complete.  Returns false (and never blocks for
 // more than kWaitLimitCycles) when the wait gives up or another role of the CTA raised *abort.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
@@ -56,8 +71,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const long long t0 = clock64();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_sleep(bar, parity)) return true;
     if (*abort) return false;
     if (clock64() - t0 > kWaitLimitCycles) return false;
   }

@@ -47,13 +47,24 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 // Bounded wait with cluster-scope acquire (for barriers that receive arrivals from the peer).
+__device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait_cluster(bar, parity)) return true;
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_cluster_sleep(bar, parity)) return true;
     if (*abort) return false;
     if (clock64() - t0 > kWaitLimitCycles) return false;
   }

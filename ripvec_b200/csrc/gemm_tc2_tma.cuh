@@ -238,12 +238,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2TmaCfg::kThread
       const bool live = row < M;
       const int b = q % Cfg::kRing;
       uint8_t* buf = ring_e + b * Cfg::kRingBytes;
-      if (e0) {
-        // The store that last used slot b (group q - kRing) has read its tile; when C is read, the
-        // slot of group q + 1 (that of q - 1 with two slots) must be free as well.
-        if (Epi::kReadsC) bulk_wait_read<0>();
-        else bulk_wait_read<Cfg::kRing - 1>();
-        if (Epi::kReadsC && q + 1 < total_groups) {
+      if (e0 && Epi::kReadsC && q + 1 < total_groups) {
+        // C of group q + 1 goes into slot (q + 1) % 2, which group q - 1's store reads.
+        bulk_wait_read<0>();
+        {
           const int qn = q + 1, tn = group_tile(qn), bn = qn % Cfg::kRing;
           fence_proxy_async();
           mbar_arrive_expect_tx(&rfull_e[bn], Cfg::kRingBytes);
@@ -291,6 +289,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2TmaCfg::kThread
         }
       }
       fence_proxy_async();
+      // Group q + 1 overwrites slot (q + 1) % 2 = (q - 1) % 2 as soon as this barrier opens, so the
+      // store of group q - 1 must have read it before (stores up to q - 1 are the outstanding ones).
+      if (e0) bulk_wait_read<0>();
       if (epi_bar_any(bar_id, fail || *abort_flag != 0)) {
         ok = false;
         break;
