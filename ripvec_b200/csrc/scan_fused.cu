@@ -25,6 +25,26 @@ constexpr int kFilterMaxKp = 512;  // larger candidate lists use the chunked pat
 
 constexpr int kFilterMaxThr = 2048;  // staged thresholds (queries); the CTA's counter follows
 
+// Writes the records of the set bits of (m0, m1) (columns col + bit, bit 32+ for m1) from vals
+// into rec[p0...] (slots past cap are dropped).  Out of line: one copy serves every call site of
+// the filter epilogue, which keeps the GEMM's instruction footprint small.
+__device__ __noinline__ void write_records(int4* rec, int cap, int p0, const float* vals, uint32_t m0,
+                                           uint32_t m1, int col, int row) {
+  int p = p0;
+  while (m0) {
+    const int i = __ffs(m0) - 1;
+    m0 &= m0 - 1;
+    if (p < cap) rec[p] = make_int4(col + i, row, __float_as_int(vals[i]), 0);
+    ++p;
+  }
+  while (m1) {
+    const int i = __ffs(m1) - 1;
+    m1 &= m1 - 1;
+    if (p < cap) rec[p] = make_int4(col + 32 + i, row, __float_as_int(vals[32 + i]), 0);
+    ++p;
+  }
+}
+
 // Epilogue of the filtering GEMM: row = database row of the block, col = query.  The negated
 // thresholds of all queries and the CTA's record counter live in the staging shared memory.  A
 // kept score becomes a {query, block row, score bits} record in the CTA's own region of `rec`;
@@ -49,10 +69,6 @@ struct EpiTopKFilter {
   }
   __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
   __device__ __forceinline__ void load(Pre&, int, int) const {}
-  __device__ __forceinline__ void put(int p, int q, float v, int row) const {
-    if (p < rec_cap)
-      rec[static_cast<size_t>(blockIdx.x) * rec_cap + p] = make_int4(q, row, __float_as_int(v), 0);
-  }
   __device__ __forceinline__ void finish(int t) const {
     if (t == 0) rec_n[blockIdx.x] = *cnt_s;
   }
@@ -78,11 +94,17 @@ struct EpiTopKFilter {
     const unsigned am = __activemask();
     const bool hit = fmaxf(margin32(v0, nt), margin32(v1, nt + 8)) > 0.f;
     if (!__any_sync(am, hit)) return;  // common case: nothing in these 64 columns passes
-    // Slots for the warp's records: per-lane counts, a warp prefix sum, one shared atomic.
-    int cnt = 0;
+    // Masks of the passing columns, then slots for the warp's records: per-lane counts, a warp
+    // prefix sum, one shared atomic.
+    uint32_t m0 = 0u, m1 = 0u;
+    if (hit) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      cnt += (v0[i] > -nthr_s[col + i] ? 1 : 0) + (v1[i] > -nthr_s[col + 32 + i] ? 1 : 0);
+      for (int i = 0; i < 32; ++i) {
+        m0 |= (v0[i] > -nthr_s[col + i] ? 1u : 0u) << i;
+        m1 |= (v1[i] > -nthr_s[col + 32 + i] ? 1u : 0u) << i;
+      }
+    }
+    const int cnt = __popc(m0) + __popc(m1);
     const int lane = threadIdx.x & 31;
     const int last = 31 - __clz(am);
     int incl = cnt;
@@ -95,12 +117,14 @@ struct EpiTopKFilter {
     if (lane == last) base = atomicAdd(cnt_s, incl);
     base = __shfl_sync(am, base, last);
     if (cnt == 0) return;
-    int p = base + incl - cnt;
+    float vals[64];  // local copy: the writer below indexes it by bit position
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      if (v0[i] > -nthr_s[col + i]) put(p++, col + i, v0[i], row);
-      if (v1[i] > -nthr_s[col + 32 + i]) put(p++, col + 32 + i, v1[i], row);
+      vals[i] = v0[i];
+      vals[32 + i] = v1[i];
     }
+    write_records(rec + static_cast<size_t>(blockIdx.x) * rec_cap, rec_cap, base + incl - cnt, vals,
+                  m0, m1, col, row);
   }
 };
 
