@@ -115,14 +115,19 @@ __device__ __forceinline__ int half_class(int kb, int L, int qa, int qb, int wh)
 }
 
 // Masks (class 1) the 32 scores of keys kb..kb+31 for query qi to -inf and returns their max.
+// The visible keys of a row form one interval [max(0, qi - wh), min(L - 1, qi + wh)] (wh < 0:
+// [0, L - 1]); its intersection with the half is turned into a 32-bit mask with a few integer
+// operations, then each score costs one bit test and one select.
 __device__ __forceinline__ float masked_max(float (&s)[32], int cls, int kb, int L, int qi, int wh) {
   if (cls == 1) {
+    const int lo = max(wh < 0 ? 0 : qi - wh, 0) - kb;           // first visible offset
+    const int hi = min(wh < 0 ? L - 1 : qi + wh, L - 1) - kb;   // last visible offset
+    const int a = max(lo, 0), b = min(hi, 31);
+    // bits a..b set (none when a > b)
+    const uint32_t vis = a > b ? 0u : ((0xffffffffu >> (31 - b)) & (0xffffffffu << a));
 #pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      const int k = kb + c;
-      const bool vis = k < L && (wh < 0 || abs(qi - k) <= wh);
-      if (!vis) s[c] = -INFINITY;
-    }
+    for (int c = 0; c < 32; ++c)
+      if (!((vis >> c) & 1u)) s[c] = -INFINITY;
   }
   float mx[4] = {fmax3(s[0], s[1], s[2]), fmax3(s[3], s[4], s[5]), fmax3(s[6], s[7], s[8]),
                  fmax3(s[9], s[10], s[11])};
