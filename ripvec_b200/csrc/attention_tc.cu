@@ -34,8 +34,10 @@ namespace {
 constexpr int kBQ = 128;       // queries per item
 constexpr int kBKV = 64;       // keys per tile
 constexpr int kD = 64;         // head dim
-constexpr int kKStages = 2;
-constexpr int kVStages = 3;
+// K is on the critical path (S of tile g + 2 needs it) and is loaded kKStages tiles ahead; V
+// is needed only when P V is issued.
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
 constexpr int kQBytes = kBQ * kD * 2;    // 16 KB
 constexpr int kKVBytes = kBKV * kD * 2;  // 8 KB
 constexpr int kPBytes = kBQ * kBKV * 2;  // 16 KB
@@ -234,16 +236,16 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
   uint64_t* bar = reinterpret_cast<uint64_t*>(xsum + 2 * 2 * kBQ);
   uint64_t* q_full = bar;          // [2] Q landed
   uint64_t* q_empty = bar + 2;     // [2] last S MMA of the item that read Q completed
-  uint64_t* k_full = bar + 4;      // [kKStages]
-  uint64_t* k_empty = bar + 6;     // [kKStages] S MMA that read the K tile completed
-  uint64_t* v_full = bar + 8;      // [kVStages]
-  uint64_t* v_empty = bar + 11;    // [kVStages] P V MMA that read the V tile completed
-  uint64_t* s_full = bar + 14;     // [2] scores in TMEM
-  uint64_t* p_full = bar + 16;     // [2] P written (and the scores read) by the 8 softmax warps
-  uint64_t* p_empty = bar + 18;    // [2] P V MMA of the tile completed (P slot free, O updated)
-  uint64_t* o_empty = bar + 20;    // [2] an item's O read out by the 8 softmax warps
-  uint64_t* drain = bar + 22;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 25);
+  uint64_t* k_full = bar + 4;                 // [kKStages]
+  uint64_t* k_empty = k_full + kKStages;      // [kKStages] S MMA that read the K tile completed
+  uint64_t* v_full = k_empty + kKStages;      // [kVStages]
+  uint64_t* v_empty = v_full + kVStages;      // [kVStages] P V MMA that read the V tile completed
+  uint64_t* s_full = v_empty + kVStages;      // [2] scores in TMEM
+  uint64_t* p_full = s_full + 2;              // [2] P written (and the scores read) by the 8 softmax warps
+  uint64_t* p_empty = p_full + 2;             // [2] P V MMA of the tile completed (P slot free, O updated)
+  uint64_t* o_empty = p_empty + 2;            // [2] an item's O read out by the 8 softmax warps
+  uint64_t* drain = o_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -278,21 +280,29 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  static_assert(kKStages == 2 && kVStages == 3, "barrier offsets assume 2 K and 3 V stages");
+  static_assert((13 + 2 * (kKStages + kVStages)) * 8 + 8 <= 512, "barrier area");
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
+    // ---------------------------------------------------------------- TMA producers
+    // Lane 0 loads Q and K, lane 1 loads V; each walks the same tile sequence with its own ring,
+    // so a V slot that is still being read never holds back the next K load.
+    if (lane < 2) {
+      const bool kq = lane == 0;
       Walk wk;
       wk.init(tiles, n_tiles, n_items, window_half);
       bool ok = true;
       // Per-slot record of issued loads (bit = slot issued, parity of its last phase), so that an
       // aborting CTA can let them land before it exits.
-      uint32_t q_iss = 0, q_par = 0, k_iss = 0, k_par = 0, v_iss = 0, v_par = 0;
-      int ks = 0, vs = 0;
-      uint32_t kph = 0, vph = 0;
+      uint32_t q_iss = 0, q_par = 0, iss = 0, par = 0;
+      const int stages = kq ? kKStages : kVStages;
+      uint64_t* full = kq ? k_full : v_full;
+      uint64_t* empty = kq ? k_empty : v_empty;
+      uint8_t* ring = kq ? sK : sV;
+      const int col0 = (kq ? H : 2 * H);
+      int rs = 0;
+      uint32_t rph = 0;
       while (wk.valid(n_items)) {
-        if (wk.j == 0) {
+        if (kq && wk.j == 0) {
           const int qs = wk.i & 1;
           const uint32_t qph = (wk.i >> 1) & 1;
           if (!mbar_wait(&q_empty[qs], qph ^ 1u, abort_flag)) { ok = false; break; }
@@ -304,18 +314,12 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
           q_par = (q_par & ~(1u << qs)) | (qph << qs);
         }
         const int row = wk.s0 + (wk.t_lo + wk.j) * kBKV;
-        if (!mbar_wait(&k_empty[ks], kph ^ 1u, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(&k_full[ks], kKVBytes);
-        tma_load_2d(sK + ks * kKVBytes, &tmQKV, &k_full[ks], H + wk.head(n_tiles) * kD, row);
-        k_iss |= 1u << ks;
-        k_par = (k_par & ~(1u << ks)) | (kph << ks);
-        if (++ks == kKStages) { ks = 0; kph ^= 1u; }
-        if (!mbar_wait(&v_empty[vs], vph ^ 1u, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(&v_full[vs], kKVBytes);
-        tma_load_2d(sV + vs * kKVBytes, &tmQKV, &v_full[vs], 2 * H + wk.head(n_tiles) * kD, row);
-        v_iss |= 1u << vs;
-        v_par = (v_par & ~(1u << vs)) | (vph << vs);
-        if (++vs == kVStages) { vs = 0; vph ^= 1u; }
+        if (!mbar_wait(&empty[rs], rph ^ 1u, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[rs], kKVBytes);
+        tma_load_2d(ring + rs * kKVBytes, &tmQKV, &full[rs], col0 + wk.head(n_tiles) * kD, row);
+        iss |= 1u << rs;
+        par = (par & ~(1u << rs)) | (rph << rs);
+        if (++rs == stages) { rs = 0; rph ^= 1u; }
         wk.next(tiles, n_tiles, n_items, window_half);
       }
       if (!ok) {
@@ -323,10 +327,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         atomicOr(err, kErrWaitTimeout);
         for (int b = 0; b < 2; ++b)
           if (q_iss & (1u << b)) wait_done(&q_full[b], (q_par >> b) & 1u);
-        for (int b = 0; b < kKStages; ++b)
-          if (k_iss & (1u << b)) wait_done(&k_full[b], (k_par >> b) & 1u);
-        for (int b = 0; b < kVStages; ++b)
-          if (v_iss & (1u << b)) wait_done(&v_full[b], (v_par >> b) & 1u);
+        for (int b = 0; b < stages; ++b)
+          if (iss & (1u << b)) wait_done(&full[b], (par >> b) & 1u);
       }
     }
   } else if (warp == 1) {
@@ -337,6 +339,15 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
       wp.init(tiles, n_tiles, n_items, window_half);
       int ks = 0, vs = 0;
       uint32_t kph = 0, vph = 0, gs = 0, gp = 0;
+      // Shared-memory descriptors of every ring slot, built once.  Advancing 16 keys (K-major,
+      // 32 bytes) or 16 rows (MN-major V, 2048 bytes) adds to the 16-byte address field.
+      // Slots are picked with selects (the address field is the only difference), keeping the
+      // descriptors in registers.
+      static_assert(kKStages == 3 && kVStages == 2, "slot selects below");
+      const uint64_t dq0 = smem_desc_sw128(smem_u32(sQ)), dq1 = dq0 + (kQBytes >> 4);
+      const uint64_t dp0 = smem_desc_sw128(smem_u32(sP)), dp1 = dp0 + (kPBytes >> 4);
+      const uint64_t dk0 = smem_desc_sw128(smem_u32(sK));
+      const uint64_t dv0 = smem_desc_sw128_mn(smem_u32(sV)), dv1 = dv0 + (kKVBytes >> 4);
       // S[gs & 1] = Q K^T over the 64-wide head dim (4 MMAs of K = 16).  S[gs & 1] is free: the
       // softmax warps released S of tile gs - 2 (p_full) before P V of that tile was issued.
       auto issue_s = [&]() -> bool {
@@ -344,12 +355,11 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         if (ws.j == 0 && !mbar_wait(&q_full[qs], (ws.i >> 1) & 1, abort_flag)) return false;
         if (!mbar_wait(&k_full[ks], kph, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQ + qs * kQBytes);
-        const uint32_t k_addr = smem_u32(sK + ks * kKVBytes);
+        const uint64_t aq = qs ? dq1 : dq0;
+        const uint64_t bk = dk0 + static_cast<uint64_t>(ks * (kKVBytes >> 4));
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          tc_mma_f16(tmem_base + (gs & 1) * kBKV, smem_desc_sw128(q_addr + 32 * kk),
-                     smem_desc_sw128(k_addr + 32 * kk), kIdS, kk > 0 ? 1u : 0u);
+          tc_mma_f16(tmem_base + (gs & 1) * kBKV, aq + 2 * kk, bk + 2 * kk, kIdS, kk > 0 ? 1u : 0u);
         tc_commit(&s_full[gs & 1]);
         tc_commit(&k_empty[ks]);
         if (ws.last_tile()) tc_commit(&q_empty[qs]);
@@ -373,12 +383,12 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
           break;
         }
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + b * kPBytes);
-        const uint32_t v_addr = smem_u32(sV + vs * kKVBytes);
+        const uint64_t ap = b ? dp1 : dp0;
+        const uint64_t bv = vs ? dv1 : dv0;
 #pragma unroll
         for (int kk = 0; kk < kBKV / 16; ++kk)
-          tc_mma_f16(tmem_base + 2 * kBKV + os * kD, smem_desc_sw128(p_addr + 32 * kk),
-                     smem_desc_sw128_mn(v_addr + 2048 * kk), kIdO, (wp.j > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16(tmem_base + 2 * kBKV + os * kD, ap + 2 * kk, bv + 128 * kk, kIdO,
+                     (wp.j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&v_empty[vs]);
         tc_commit(&p_empty[b]);
         if (++vs == kVStages) { vs = 0; vph ^= 1u; }
