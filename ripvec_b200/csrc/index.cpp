@@ -47,8 +47,8 @@ struct Dev {
 
 // Runs one query batch end to end on x->stream for candidate width kp.
 // Rows scored by the chunked path before the fused filter takes over (its lists give the
-// first thresholds).
-constexpr int64_t kFilterPrefixRows = 65536;
+// first thresholds): one small chunk, so that the fixed cost per query batch stays low.
+constexpr int64_t kFilterPrefixRows = 1024;
 
 // Runs one query batch end to end on x->stream for candidate width kp.  With `fused`, rows past
 // the first kFilterPrefixRows go through the filtering GEMM (scan_fused.cu) in blocks that grow
@@ -103,8 +103,9 @@ int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int k, int kp, float
     if (r0 < x->n) {
       // Fused filter over the rest.  A block of b rows after s rows seen keeps about kp * b / s
       // candidates per query on rows in random order; blocks of s rows keep about kp each, and
-      // the total over the ln(n / s0) / ln 2 blocks, 1.45 kp ln(n / s0), is about half of what
-      // fewer, larger blocks keep.
+      // the total over the log2(n / s0) blocks, 1.45 kp ln(n / s0), is about half of what fewer,
+      // larger blocks keep.  Starting from a 1024-row prefix costs a few small blocks instead of
+      // a long chunked prefix, which matters when a rank's shard is small (strong scaling).
       const int fcap = rv::scan_filter_cap();
       const int nq_pad = (nq + 255) / 256 * 256;
       const int sms = rv::device_sm_count();
@@ -117,7 +118,7 @@ int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int k, int kp, float
       if (!rv::make_tmap_2d_16bit(&tq256, qb, true, x->dim, nq, uint64_t(x->dim) * 2, 64, 256, &why))
         return ifail(x, RV_E_CUDA, why);
       while (r0 < x->n) {
-        const int64_t rows = std::min<int64_t>({x->n - r0, std::max<int64_t>(65536, r0), int64_t(1) << 24});
+        const int64_t rows = std::min<int64_t>({x->n - r0, r0, int64_t(1) << 24});
         CUtensorMap trows;
         if (!rv::make_tmap_2d_16bit(&trows, x->db + size_t(r0) * x->dim, true, x->dim, uint64_t(rows),
                                     uint64_t(x->dim) * 2, 64, 128, &why))
