@@ -40,15 +40,13 @@ constexpr int kKStages = 3;
 constexpr int kVStages = 2;
 constexpr int kQBytes = kBQ * kD * 2;    // 16 KB
 constexpr int kKVBytes = kBKV * kD * 2;  // 8 KB
-constexpr int kPBytes = kBQ * kBKV * 2;  // 16 KB
 constexpr int kTmemCols = 256;           // S[2] at columns 0, 64; O[2] at 128, 192
 constexpr int kThreads = 320;  // producer, MMA issuer, 8 softmax warps
 // Row-max / row-sum exchange between the two softmax warps of a row: max [2 tiles][2 halves][128]
 // and sum [2 items][2 halves][128] floats.
 constexpr int kXBytes = (2 * 2 * kBQ + 2 * 2 * kBQ) * 4;
-// 110 KB: two CTAs fit an SM and a third never does, so 2 x 256 TMEM columns always fit.
-constexpr int kSmem =
-    1024 + 2 * kQBytes + (kKStages + kVStages) * kKVBytes + 2 * kPBytes + kXBytes + 512;
+// 78 KB: two CTAs fit an SM; TMEM (256 columns per CTA) keeps it at two.
+constexpr int kSmem = 1024 + 2 * kQBytes + (kKStages + kVStages) * kKVBytes + kXBytes + 512;
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -71,10 +69,6 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_mn(uint32_t saddr) {
   return d;
 }
 
-__device__ __forceinline__ void fence_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // Completion wait that ignores the abort flag (bounded by time only): used on error paths to let
 // copies and MMAs already in flight finish before the CTA releases its memory.
 __device__ __forceinline__ bool wait_done(uint64_t* bar, uint32_t parity) {
@@ -85,11 +79,6 @@ __device__ __forceinline__ bool wait_done(uint64_t* bar, uint32_t parity) {
 __host__ __device__ constexpr uint32_t idesc_f16_bmn(int M, int N, bool is_bf16) {
   return idesc_f16(M, N, is_bf16) | (1u << 16);  // B operand MN-major
 }
-
-__device__ __forceinline__ uint32_t swz128(int r, int j) {
-  return static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
-}
-
 
 // Barrier of the two softmax warps of a row (named barrier `id`, 64 threads) that also ORs a
 // flag over them, so a wait that failed in either warp ends both at the same point.
@@ -138,28 +127,24 @@ __device__ __forceinline__ float masked_max(float (&s)[32], int cls, int kb, int
   return fmax3(mx[0], mx[1], fmaxf(mx[2], mx[3]));
 }
 
-// P = exp2(s * scale_log2 - m) of 32 keys as 16-bit, into 16-byte chunks c8_0..c8_0+3 of row r
-// of the swizzled P tile (zeros when the half is not visible); adds the f32 values to the two
-// packed partial sums ps.  sl2 = {scale_log2, scale_log2}, nm2 = {-m, -m}.
+// P = exp2(s * scale_log2 - m) of 32 keys as 16 packed 16-bit pairs (zeros when the half is
+// not visible); adds the f32 values to the two packed partial sums ps.  sl2 = {scale_log2,
+// scale_log2}, nm2 = {-m, -m}.
 template <typename T>
-__device__ __forceinline__ void write_p(uint8_t* pt, int r, int c8_0, bool live, const float (&s)[32],
-                                        uint64_t sl2, uint64_t nm2, uint64_t (&ps)[2]) {
+__device__ __forceinline__ void make_p(bool live, const float (&s)[32], uint64_t sl2, uint64_t nm2,
+                                       uint64_t (&ps)[2], uint32_t (&w)[16]) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t w4[4] = {0u, 0u, 0u, 0u};
+  for (int e = 0; e < 16; ++e) {
+    w[e] = 0u;
     if (live) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        // Masked scores are -inf: exp2(-inf) = 0 exactly.
-        float x0, x1;
-        f2_unpack(f2_fma(f2_pack(s[8 * c + 2 * e], s[8 * c + 2 * e + 1]), sl2, nm2), x0, x1);
-        const float p0 = ex2(x0), p1 = ex2(x1);
-        ps[e & 1] = f2_add(ps[e & 1], f2_pack(p0, p1));
-        auto v = Elem<T>::pack(p0, p1);
-        w4[e] = *reinterpret_cast<uint32_t*>(&v);
-      }
+      // Masked scores are -inf: exp2(-inf) = 0 exactly.
+      float x0, x1;
+      f2_unpack(f2_fma(f2_pack(s[2 * e], s[2 * e + 1]), sl2, nm2), x0, x1);
+      const float p0 = ex2(x0), p1 = ex2(x1);
+      ps[e & 1] = f2_add(ps[e & 1], f2_pack(p0, p1));
+      auto v = Elem<T>::pack(p0, p1);
+      w[e] = *reinterpret_cast<uint32_t*>(&v);
     }
-    *reinterpret_cast<uint4*>(pt + swz128(r, c8_0 + c)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
   }
 }
 
@@ -230,8 +215,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
   uint8_t* sQ = smem;                        // [2] x 16 KB
   uint8_t* sK = sQ + 2 * kQBytes;            // [kKStages] x 8 KB
   uint8_t* sV = sK + kKStages * kKVBytes;    // [kVStages] x 8 KB
-  uint8_t* sP = sV + kVStages * kKVBytes;    // [2] x 16 KB
-  float* xmax = reinterpret_cast<float*>(sP + 2 * kPBytes);  // [2][2][kBQ]
+  float* xmax = reinterpret_cast<float*>(sV + kVStages * kKVBytes);  // [2][2][kBQ]
   float* xsum = xmax + 2 * 2 * kBQ;                           // [2][2][kBQ]
   uint64_t* bar = reinterpret_cast<uint64_t*>(xsum + 2 * 2 * kBQ);
   uint64_t* q_full = bar;          // [2] Q landed
@@ -241,8 +225,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
   uint64_t* v_full = k_empty + kKStages;      // [kVStages]
   uint64_t* v_empty = v_full + kVStages;      // [kVStages] P V MMA that read the V tile completed
   uint64_t* s_full = v_empty + kVStages;      // [2] scores in TMEM
-  uint64_t* p_full = s_full + 2;              // [2] P written (and the scores read) by the 8 softmax warps
-  uint64_t* p_empty = p_full + 2;             // [2] P V MMA of the tile completed (P slot free, O updated)
+  uint64_t* p_full = s_full + 2;              // [2] P written over S in TMEM by the 8 softmax warps
+  uint64_t* p_empty = p_full + 2;             // [2] P V MMA of the tile completed (O updated)
   uint64_t* o_empty = p_empty + 2;            // [2] an item's O read out by the 8 softmax warps
   uint64_t* drain = o_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -345,7 +329,6 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
       // descriptors in registers.
       static_assert(kKStages == 3 && kVStages == 2, "slot selects below");
       const uint64_t dq0 = smem_desc_sw128(smem_u32(sQ)), dq1 = dq0 + (kQBytes >> 4);
-      const uint64_t dp0 = smem_desc_sw128(smem_u32(sP)), dp1 = dp0 + (kPBytes >> 4);
       const uint64_t dk0 = smem_desc_sw128(smem_u32(sK));
       const uint64_t dv0 = smem_desc_sw128_mn(smem_u32(sV)), dv1 = dv0 + (kKVBytes >> 4);
       // S[gs & 1] = Q K^T over the 64-wide head dim (4 MMAs of K = 16).  S[gs & 1] is free: the
@@ -375,20 +358,21 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         const int b = gp & 1;
         const uint32_t ph = (gp >> 1) & 1;
         const int os = wp.i & 1;  // O buffer of the item
-        // O[os] (+)= P V: P is K-major over the 64 keys, V is MN-major (keys x head dim).  An
-        // item's first tile overwrites O[os], once the item two back has been read out of it.
+        // O[os] (+)= P V: P (16-bit, written over S[b] in TMEM: 128 lanes x 32 columns) is the A
+        // operand, V is MN-major in shared memory (keys x head dim).  An item's first tile
+        // overwrites O[os], once the item two back has been read out of it.  S of tile gp + 2
+        // reuses S[b] only after this MMA, in this thread's issue order.
         if ((wp.j == 0 && !mbar_wait(&o_empty[os], ((wp.i >> 1) & 1) ^ 1u, abort_flag)) ||
             !mbar_wait(&p_full[b], ph, abort_flag) || !mbar_wait(&v_full[vs], vph, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t ap = b ? dp1 : dp0;
         const uint64_t bv = vs ? dv1 : dv0;
 #pragma unroll
         for (int kk = 0; kk < kBKV / 16; ++kk)
-          tc_mma_f16(tmem_base + 2 * kBKV + os * kD, ap + 2 * kk, bv + 128 * kk, kIdO,
-                     (wp.j > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tmem_base + 2 * kBKV + os * kD, tmem_base + b * kBKV + 8 * kk, bv + 128 * kk,
+                        kIdO, (wp.j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&v_empty[vs]);
         tc_commit(&p_empty[b]);
         if (++vs == kVStages) { vs = 0; vph ^= 1u; }
@@ -489,15 +473,19 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
           }
         }
         if (!fail) {
-          uint8_t* pt = sP + b * kPBytes;
+          // P of this half's 32 keys, as 16 packed pairs, over the first half of S[b]: both
+          // warps of the row loaded their scores before the exchange barrier above, so this
+          // store cannot overwrite scores still to be read.
           const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m, -m);
           uint64_t ps[2] = {0ull, 0ull};  // two packed partial sums (f32 zero bits)
-          write_p<T>(pt, r, 4 * half, cls != 0, sv, sl2, nm2, ps);
+          uint32_t w[16];
+          make_p<T>(cls != 0, sv, sl2, nm2, ps, w);
+          tmem_st16(trow + b * kBKV + 16 * half, w);
           float p0, p1, p2, p3;
           f2_unpack(ps[0], p0, p1);
           f2_unpack(ps[1], p2, p3);
           l += (p0 + p1) + (p2 + p3);
-          fence_async_smem();  // generic-proxy stores -> visible to the tensor core
+          tc_wait_st();  // P is in TMEM before the MMA thread may read it
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&p_full[b]);
