@@ -1,25 +1,27 @@
 // Varlen attention on the 5th-generation tensor cores (head_dim 64, bf16 or f16).
 //
 // Work item = (128-query tile of one sequence, head); the host lists the tiles as
-// {sequence start, length, first query} records.  The kernel is persistent: two CTAs per SM each
-// walk the items blockIdx.x, blockIdx.x + gridDim.x, ... (head-major, so the items in flight
-// share their sequences' K/V in L2), and every ring below runs across item boundaries, so the
-// next item's Q and K/V load while the current one finishes.  Warp roles (192 threads):
-//   warp 0      TMA producer: Q per item (2 buffers), K tiles (2-deep ring) and V tiles (3-deep)
-//               of 64 keys,
+// {sequence start, length | first query << 16} records.  The kernel is persistent: two CTAs per
+// SM each walk the items blockIdx.x, blockIdx.x + gridDim.x, ... (head-major, so the items in
+// flight share their sequences' K/V in L2), and every ring below runs across item boundaries,
+// so the next item's Q and K/V load while the current one finishes.  Warp roles (320 threads):
+//   warp 0      TMA producers: lane 0 loads Q per item (2 buffers) and K tiles (3-deep ring),
+//               lane 1 loads V tiles (2-deep ring), 64 keys per tile,
 //   warp 1      TMEM owner and single-thread tcgen05.mma issuer,
-//   warps 2..5  softmax: thread r owns query row r (= TMEM lane r).
+//   warps 2..9  softmax: warps w and w + 4 share TMEM lane quadrant w % 4 (query rows) and take
+//               32 keys each of every tile.
 // Per key tile g (counted across items):
 //   S[g&1] = Q K^T      tcgen05.mma M=128 N=64 K=64 into TMEM, issued two tiles ahead,
-//   softmax             each thread reads its 64 scores with tcgen05.ld, masks keys past the
-//                       sequence end and, on sliding-window layers, keys with |i - j| > w/2;
-//                       keeps the running max and sum in f32 and writes P = exp2(s - m) as
-//                       16-bit into a 128-byte-swizzled shared tile.  32-key halves that no row
-//                       of the warp can see skip the exponentials,
-//   O[g&1] = P V        tcgen05.mma M=128 N=64 K=64 with V as an MN-major operand,
-//   accumulate          O_reg = O_reg * alpha + O[g&1] in registers, one tile behind, so the
-//                       P V MMA overlaps the next tile's softmax; the last fold of an item
-//                       writes its context rows.
+//   softmax             each thread reads its 32 scores with tcgen05.ld, masks keys past the
+//                       sequence end and, on sliding-window layers, keys with |i - j| > w/2
+//                       (32-key halves that no row of the warp can see skip the exponentials);
+//                       the two warps of a row exchange their maxima; P = exp2(s - m) is
+//                       written as packed 16-bit pairs over S[g&1] in TMEM (tcgen05.st),
+//   O += P V            tcgen05.mma M=128 N=64 K=64 with P (A) read from TMEM and V as an
+//                       MN-major shared-memory operand, into the item's TMEM accumulator; the
+//                       reference max m moves only when a row's max grows by more than 2^8
+//                       (then the row's O is rescaled in TMEM), and the item's context rows are
+//                       written after the next item's first tile.
 // Reference semantics: backend/arch/modern_bert.rs:250-322 and driver/cpu.rs:1016-1074 (scores *
 // 1/sqrt(d), additive -1e9 masks for padding and |i-j| > window/2, max-subtracted softmax, P V);
 // masked keys get weight 0 exactly, as exp(-1e9 - max) does in f32.

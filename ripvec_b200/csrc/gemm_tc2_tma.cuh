@@ -1,13 +1,15 @@
 // Two-CTA tcgen05 GEMM with a TMA-staged epilogue (the encoder's projection GEMMs).
 //
-// Mainloop as gemm_tc2_kernel (cta_group::2, 256 x 256 pair tiles, 5 stages of 32 KB per CTA).
-// Epilogue: the 128 x 256 accumulator block of each CTA is processed in four 64-column groups
-// through a ring of three 16 KB shared-memory tiles.  When the epilogue reads the output as well
-// (residual add), one thread TMA-loads the next group's 128 x 64 block of C into the ring one
-// group ahead; every thread then combines its row with its accumulator columns, writes the result
-// into the same tile (128-byte swizzled, bank-conflict free), and after a named barrier the same
-// thread TMA-stores the tile.  Epilogue threads never wait on global memory; the accumulator is
-// released as soon as the last TMEM load of a tile is done.
+// Mainloop as gemm_tc2_kernel (cta_group::2, 256 x 256 pair tiles, 4 stages of 32 KB per CTA)
+// into two TMEM accumulators.  Epilogue: two warpgroups of 128 threads, warpgroup e draining
+// accumulator e (every other tile), so two tiles' epilogues run at once.  Each processes its
+// 128 x 256 block in four 64-column groups through its own ring of two 16 KB shared-memory
+// tiles.  When the epilogue reads the output as well (residual add), one thread TMA-loads the
+// next group's 128 x 64 block of C into the ring one group ahead; every thread then combines its
+// row with its accumulator columns, writes the result into the same tile (128-byte swizzled,
+// bank-conflict free), and after a named barrier the same thread TMA-stores the tile.  Epilogue
+// threads never wait on global memory; the accumulator is released as soon as the last TMEM load
+// of a tile is done.
 #pragma once
 
 #include "gemm_epi_tma.cuh"
