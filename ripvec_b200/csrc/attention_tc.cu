@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         // overwrites O[os], once the item two back has been read out of it.  S of tile gp + 2
         // reuses S[b] only after this MMA, in this thread's issue order.
         if ((wp.j == 0 && !mbar_wait(&o_empty[os], ((wp.i >> 1) & 1) ^ 1u, abort_flag)) ||
-            !mbar_wait(&p_full[b], ph, abort_flag) || !mbar_wait(&v_full[vs], vph, abort_flag)) {
+            !mbar_wait_spin(&p_full[b], ph, abort_flag) || !mbar_wait(&v_full[vs], vph, abort_flag)) {
           ok = false;
           break;
         }
