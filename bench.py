@@ -59,6 +59,9 @@ def parse_args():
     ap.add_argument("--max-batch-tokens", type=int, default=1 << 19)
     ap.add_argument("--scan-rows", type=int, default=10_000_000,
                     help="database rows of the scan workload (smaller only for profiling)")
+    ap.add_argument("--queries", default="1024",
+                    help="queries per step of the scan workload, or a comma-separated list (one JSON line "
+                         "each, same database); the roofline is HBM below ~210 queries, tensor above")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -436,8 +439,6 @@ def run_encoder(args):
 
 
 def run_scan(args):
-    import ctypes as C
-
     import torch
 
     from ripvec_b200 import synth
@@ -452,7 +453,7 @@ def run_scan(args):
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    n_rows, dim, nq, k = args.scan_rows, 768, 1024, 100
+    n_rows, dim, k = args.scan_rows, 768, 100
     from ripvec_b200 import shard as shard_mod
 
     lo, hi = shard_mod.row_ranges(n_rows, world)[rank]
@@ -465,11 +466,23 @@ def run_scan(args):
         shard[s:e] = (x / x.norm(dim=1, keepdim=True)).to(torch.bfloat16)
     idx = SearchIndex(shard, device=local, base=lo)
     del shard
+    stream = torch.cuda.current_stream()
+    # The database shard (15.4 GB at 10M rows on one GPU) is larger than L2, so every step
+    # streams it from HBM: no flush is needed between steps.
+    for nq in [int(v) for v in str(args.queries).split(",")]:
+        scan_line(args, torch, dist, idx, merge_topk_device, synth, stream, rank, world, local,
+                  n_rows, dim, nq, k)
+    idx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def scan_line(args, torch, dist, idx, merge_topk_device, synth, stream, rank, world, local, n_rows, dim, nq, k):
+    """Times ``args.steps`` exact top-k steps of ``nq`` queries and prints one JSON line (rank 0)."""
     q = torch.from_numpy(synth.normalized_gaussian(nq, dim, seed=99)).cuda()
     oi = torch.empty(nq, k, dtype=torch.int64, device="cuda")
     os_ = torch.empty(nq, k, dtype=torch.float32, device="cuda")
     o64 = torch.empty(nq, k, dtype=torch.float64, device="cuda")
-    stream = torch.cuda.current_stream()
 
     def step():
         idx.topk_device(q, k, oi, os_, o64, stream=stream.cuda_stream)
@@ -486,39 +499,53 @@ def run_scan(args):
     if dist is not None:
         dist.barrier()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(physical_gpu(local))
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
     for s in range(args.steps):
         evs[s][0].record(stream)
         step()
         evs[s][1].record(stream)
     torch.cuda.synchronize()
+    clocks = sampler.stop() if rank == 0 else None
     ms = sum(a.elapsed_time(b) for a, b in evs)
     if dist is not None:
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    if rank == 0:
-        pk = peaks()
-        db_bytes = (n_rows // world) * dim * 2
-        line = {"metric": "exact cosine top-100 queries/sec (10M x 768 bf16)", "value": nq * args.steps / (ms / 1e3),
-                "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "bf16", "data": "synthetic normalised Gaussian rows",
-                "config": {"workload": "scan_topk", "rows": n_rows, "dim": dim, "queries": nq, "k": k,
-                           "parallelism": f"rows{world}"},
-                "db_gbs_per_rank": db_bytes / (ms / args.steps / 1e3) / 1e9, "hbm_peak_gbs": pk["hbm_gbs"]}
-        # With 1024 queries every database byte feeds 1024 multiply-adds: the scan is bound by the
-        # tensor cores (2 * nq * rows * dim FLOP per step per rank), not by HBM.
-        flops = 2.0 * nq * (n_rows // world) * dim
-        ach = flops / (ms / args.steps / 1e3) / 1e12
-        line["roofline"] = {"kernel": "scan step (fused tcgen05 filter GEMM + merges + exact rescoring)",
-                            "bound": "tensor", "achieved": ach, "peak": pk["bf16_sus"], "unit": "TFLOP/s",
-                            "frac": ach / pk["bf16_sus"],
+    if rank != 0:
+        return
+    pk = peaks()
+    db_bytes = (n_rows // world) * dim * 2
+    line = {"metric": "exact cosine top-100 queries/sec (10M x 768 bf16)", "value": nq * args.steps / (ms / 1e3),
+            "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic normalised Gaussian rows",
+            "config": {"workload": "scan_topk", "rows": n_rows, "dim": dim, "queries": nq, "k": k,
+                       "parallelism": f"rows{world}", "l2": "database shard larger than L2, no flush"},
+            "db_gbs_per_rank": db_bytes / (ms / args.steps / 1e3) / 1e9, "hbm_peak_gbs": pk["hbm_gbs"],
+            "clocks": clocks}
+    # Every database byte feeds nq / 2 multiply-adds.  Above the ridge point (peak FLOP/s over
+    # HBM bytes/s, about 213 FLOP per byte here, i.e. ~210 queries) the scan is bound by the
+    # tensor cores (2 * nq * rows * dim FLOP per step per rank); below it by streaming the
+    # database shard from HBM once per step (rows * dim * 2 bytes).
+    flops = 2.0 * nq * (n_rows // world) * dim
+    sec = ms / args.steps / 1e3
+    kern = "scan step (fused tcgen05 filter GEMM + merges + exact rescoring)"
+    if flops / db_bytes > pk["bf16_sus"] * 1e12 / (pk["hbm_gbs"] * 1e9):
+        ach = flops / sec / 1e12
+        line["roofline"] = {"kernel": kern, "bound": "tensor", "achieved": ach, "peak": pk["bf16_sus"],
+                            "unit": "TFLOP/s", "frac": ach / pk["bf16_sus"],
                             "peak_source": f"{pk['source']} bf16_tflops_sustained",
                             "traffic": None, "flops_per_step": flops}
-        print(json.dumps(line), flush=True)
-    idx.close()
-    if dist is not None:
-        dist.destroy_process_group()
+    else:
+        ach = db_bytes / sec / 1e9
+        line["roofline"] = {"kernel": kern, "bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"],
+                            "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
+                            "peak_source": f"{pk['source']} hbm_gbs", "traffic": None,
+                            "bytes_per_step": db_bytes}
+    print(json.dumps(line), flush=True)
 
 
 def main():

@@ -54,7 +54,10 @@ constexpr int64_t kFilterPrefixRows = 1024;
 // the first kFilterPrefixRows go through the filtering GEMM (scan_fused.cu) in blocks that grow
 // with the rows already seen; *x->overflow is set if a block kept more candidates than the
 // buffers hold, and the caller then redoes the batch without it.
-int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int k, int kp, float threshold,
+// qb holds nq_rows >= nq rows (a whole number of query tiles, zero past nq), so no TMA box of
+// the query operand reaches past the buffer: boxes that were mostly out of bounds (zero-filled
+// by the copy engine) made 1-64-query scans about 1.5x slower than 128-query ones.
+int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int nq_rows, int k, int kp, float threshold,
               int64_t* out_i, float* out_s, double* out_s64, bool fused) {
   cudaStream_t st = x->stream;
   if (!x->list_s.reserve(size_t(nq) * kp) || !x->list_i.reserve(size_t(nq) * kp) ||
@@ -66,7 +69,7 @@ int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int k, int kp, float
   if (x->n > 0) {
     CUtensorMap tq;
     std::string why;
-    if (!rv::make_tmap_2d_16bit(&tq, qb, true, x->dim, nq, uint64_t(x->dim) * 2, 64, 128, &why))
+    if (!rv::make_tmap_2d_16bit(&tq, qb, true, x->dim, nq_rows, uint64_t(x->dim) * 2, 64, 128, &why))
       return ifail(x, RV_E_CUDA, why);
     // Chunk schedule: the first chunk fits the select buffer with an empty list; later chunks
     // grow with the rows already seen so the expected number of survivors stays well below
@@ -107,23 +110,29 @@ int topk_pass(rv_index* x, const __nv_bfloat16* qb, int nq, int k, int kp, float
       // larger blocks keep.  Starting from a 1024-row prefix costs a few small blocks instead of
       // a long chunked prefix, which matters when a rank's shard is small (strong scaling).
       const int fcap = rv::scan_filter_cap();
-      const int nq_pad = (nq + 255) / 256 * 256;
+      const int bn = rv::scan_filter_bn(nq);
+      const int nq_pad = (nq + bn - 1) / bn * bn;
       const int sms = rv::device_sm_count();
       if (!x->thr.reserve(size_t(nq_pad)) || !x->cand_n.reserve(size_t(nq)) ||
           !x->cand_s.reserve(size_t(nq) * fcap) || !x->cand_i.reserve(size_t(nq) * fcap) ||
           !x->rec_n.reserve(size_t(sms)) ||
           !x->rec.reserve(size_t(sms) * size_t(rv::scan_filter_record_cap())))
         return ifail(x, RV_E_NOMEM, "scan filter buffer allocation failed");
-      CUtensorMap tq256;  // B operand: 256 query rows per tile
-      if (!rv::make_tmap_2d_16bit(&tq256, qb, true, x->dim, nq, uint64_t(x->dim) * 2, 64, 256, &why))
+      CUtensorMap tqb;  // B operand: bn query rows per tile
+      if (!rv::make_tmap_2d_16bit(&tqb, qb, true, x->dim, nq_rows, uint64_t(x->dim) * 2, 64, bn, &why))
         return ifail(x, RV_E_CUDA, why);
+      // Small batches with lists of at most 256 grow the blocks 5x instead of 2x: their merges are
+      // cheap, and fewer blocks mean fewer launches and partial last waves per pass over the
+      // database (a block of 4s rows after s seen keeps about 4 kp <= 1024 candidates per query,
+      // inside the 2048-entry buffer).
+      const int64_t grow = (nq <= 128 && kp <= 256) ? 4 : 1;
       while (r0 < x->n) {
-        const int64_t rows = std::min<int64_t>({x->n - r0, r0, int64_t(1) << 24});
+        const int64_t rows = std::min<int64_t>({x->n - r0, grow * r0, int64_t(1) << 24});
         CUtensorMap trows;
         if (!rv::make_tmap_2d_16bit(&trows, x->db + size_t(r0) * x->dim, true, x->dim, uint64_t(rows),
                                     uint64_t(x->dim) * 2, 64, 128, &why))
           return ifail(x, RV_E_CUDA, why);
-        IX_TRY(x, rv::scan_filter_block(trows, tq256, static_cast<int>(rows), x->dim, x->base + r0, nq,
+        IX_TRY(x, rv::scan_filter_block(trows, tqb, static_cast<int>(rows), x->dim, x->base + r0, nq,
                                         nq_pad, kp, x->thr.p, x->rec.p, x->rec_n.p, x->cand_n.p,
                                         x->cand_s.p, x->cand_i.p,
                                         x->list_s.p, x->list_i.p, x->list_n.p, x->overflow.p, x->d_err,
@@ -148,8 +157,13 @@ int topk_device(rv_index* x, const float* q_dev, int nq, int k, float threshold,
   if (nq <= 0) return RV_OK;
   if (k <= 0 || k > 2048) return ifail(x, RV_E_INVALID, "k must be in [1, 2048]");
   cudaStream_t st = x->stream;
-  if (!x->qb.reserve(size_t(nq) * x->dim)) return ifail(x, RV_E_NOMEM, "query buffer");
+  // Query rows padded with zeros to whole tiles of the filter GEMM (128 rows up to 128 queries,
+  // else 256).
+  const int nq_rows = nq <= 128 ? 128 : (nq + 255) / 256 * 256;
+  if (!x->qb.reserve(size_t(nq_rows) * x->dim)) return ifail(x, RV_E_NOMEM, "query buffer");
   IX_TRY(x, rv::scan_round_queries(q_dev, x->qb.p, int64_t(nq) * x->dim, st));
+  if (nq_rows > nq)
+    IX_TRY(x, cudaMemsetAsync(x->qb.p + size_t(nq) * x->dim, 0, size_t(nq_rows - nq) * x->dim * 2, st));
   x->launches++;
   int kp = std::max(128, 2 * k);
   // The fused filter needs the thresholds of all queries in shared memory.
@@ -158,7 +172,7 @@ int topk_device(rv_index* x, const float* q_dev, int nq, int k, float threshold,
   for (;;) {
     const bool use_fused = fused && kp <= rv::scan_filter_max_kp();
     IX_TRY(x, cudaMemsetAsync(x->overflow.p, 0, sizeof(int), st));
-    int rc = topk_pass(x, x->qb.p, nq, k, kp, threshold, out_i, out_s, out_s64, use_fused);
+    int rc = topk_pass(x, x->qb.p, nq, nq_rows, k, kp, threshold, out_i, out_s, out_s64, use_fused);
     if (rc) return rc;
     std::vector<int> g(nq);
     unsigned int e = 0;

@@ -30,9 +30,11 @@ int scan_filter_cap();
 int scan_filter_max_kp();
 int scan_filter_max_queries();
 int scan_filter_record_cap();
+// Query columns per filter GEMM tile for a batch of nq queries (128 or 256).
+int scan_filter_bn(int nq);
 // Scores database rows [row0, row0 + rows) (tm_rows: their [rows, dim] bf16 view, box 64 x 128)
-// against the queries (tm_queries: [nq, dim] bf16, box 64 x 256, read as nq_pad rows, nq_pad a
-// multiple of 256 and <= scan_filter_max_queries()), keeps scores above each query's current
+// against the queries (tm_queries: [nq, dim] bf16, box 64 x scan_filter_bn(nq), read as nq_pad
+// rows, nq_pad a multiple of scan_filter_bn(nq) and <= scan_filter_max_queries()), keeps scores above each query's current
 // kp-th list score, and merges them into the lists.  thr: [nq_pad]; rec: [sms, record cap];
 // rec_n: [sms]; cand_*: [nq, scan_filter_cap()].  *overflow is set when a CTA or a query kept
 // more candidates than its buffer holds (the lists are then incomplete).

@@ -1,7 +1,8 @@
 // Fused candidate filter of the exact top-k scan.
 //
 // After a first block of rows has given every query a candidate list of kp rows, the rest of
-// the database is scored by the tcgen05 GEMM (128 x 256 tiles) with A = database rows (each row
+// the database is scored by the tcgen05 GEMM (128 x 256 tiles; 128 x 128 for batches of at most
+// 128 queries) with A = database rows (each row
 // tile read from HBM once) and B = the bf16 queries (L2-resident), and the epilogue keeps only what can still
 // matter: a score strictly above the query's current kp-th best f32 score is appended to that
 // query's candidate buffer.  Nothing else leaves the SM, so no score matrix is written.  After
@@ -218,6 +219,10 @@ int scan_filter_cap() { return 2048; }
 int scan_filter_max_kp() { return kFilterMaxKp; }
 int scan_filter_max_queries() { return kFilterMaxThr; }
 int scan_filter_record_cap() { return 32768; }
+// A batch of at most 128 queries fills one 128-column tile: half the tensor-core work of a
+// 256-column tile whose other half would score padding, which keeps the small-batch scan bound
+// by the database stream from HBM.
+int scan_filter_bn(int nq) { return nq <= 128 ? 128 : 256; }
 
 cudaError_t scan_filter_block(const CUtensorMap& tm_rows, const CUtensorMap& tm_queries, int rows,
                               int dim, int64_t row0, int nq, int nq_pad, int kp, float* thr,
@@ -225,18 +230,21 @@ cudaError_t scan_filter_block(const CUtensorMap& tm_rows, const CUtensorMap& tm_
                               float* list_s, int64_t* list_i, int* list_n, int* overflow,
                               unsigned int* err, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  if (nq_pad % 256 != 0 || nq_pad > kFilterMaxThr || nq > nq_pad || dim % 64 != 0 || kp > kFilterMaxKp)
+  const int bn = scan_filter_bn(nq);
+  if (nq_pad % bn != 0 || nq_pad > kFilterMaxThr || nq > nq_pad || dim % 64 != 0 || kp > kFilterMaxKp)
     return cudaErrorInvalidValue;
   const int cap = scan_filter_cap();
   const int rec_cap = scan_filter_record_cap();
   const int sms = device_sm_count();
   filter_prepare_kernel<<<(nq_pad + 255) / 256, 256, 0, st>>>(list_s, list_n, kp, nq, nq_pad, thr, cand_n);
   EpiTopKFilter epi{thr, rec, rec_n, rec_cap, nq_pad};
-  cudaError_t e = launch_gemm_tc<__nv_bfloat16, 256>(tm_rows, tm_queries, rows, nq_pad, dim, 0, epi,
-                                                      err, sms, st);
+  cudaError_t e = bn == 128 ? launch_gemm_tc<__nv_bfloat16, 128>(tm_rows, tm_queries, rows, nq_pad, dim, 0,
+                                                                  epi, err, sms, st)
+                            : launch_gemm_tc<__nv_bfloat16, 256>(tm_rows, tm_queries, rows, nq_pad, dim, 0,
+                                                                  epi, err, sms, st);
   if (e != cudaSuccess) return e;
   // The GEMM ran min(tiles, sms) persistent CTAs (launch_gemm_tc), each of which wrote rec_n.
-  const int64_t tiles = (int64_t(rows) + kGemmBM - 1) / kGemmBM * (nq_pad / 256);
+  const int64_t tiles = (int64_t(rows) + kGemmBM - 1) / kGemmBM * (nq_pad / bn);
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   filter_bucket_kernel<<<grid, 256, 0, st>>>(rec, rec_n, rec_cap, row0, cap, cand_n, cand_s, cand_i,
                                              overflow);

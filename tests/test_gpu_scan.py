@@ -51,6 +51,19 @@ def test_fused_filter_many_queries_bit_exact(cuda_device):
     np.testing.assert_array_equal(cnt, ec)
 
 
+@pytest.mark.parametrize("n,dim,nq,k", [(300_000, 128, 1, 100), (30_000, 64, 128, 64), (30_000, 64, 129, 10)])
+def test_fused_filter_small_batches_bit_exact(cuda_device, n, dim, nq, k):
+    """Batches of at most 128 queries use 128-column filter tiles and blocks that grow 5x; 129
+    queries take the 256-column tiles.  Bit-exact against the oracle either way."""
+    db = synth.normalized_gaussian(n, dim, seed=17 + nq)
+    q = synth.normalized_gaussian(nq, dim, seed=18 + nq)
+    ei, es, ec = scan.topk_exact(db, q, k)
+    oi, os_, cnt, o64 = SearchIndex(db).topk(q, k, with_f64=True)
+    np.testing.assert_array_equal(oi, ei)
+    np.testing.assert_array_equal(o64, es)
+    np.testing.assert_array_equal(cnt, ec)
+
+
 def test_fused_filter_overflow_falls_back(cuda_device):
     """Every row after the prefix is a near copy of the query, so each filter block keeps far more
     candidates than its buffer: the batch is redone on the chunked path and stays exact."""
