@@ -163,6 +163,39 @@ int rv_index_topk_noalloc(rv_index* idx, const float* queries_dev, int32_t nq, i
                           float threshold, int64_t* out_idx_dev, float* out_score_dev,
                           double* out_score64_dev, void* stream);
 
+/* ---------------------------------------------------------------- PolarQuant ("TurboQuant") search
+ * The approximate first phase of SearchIndex::rank_turboquant (crates/ripvec-core/src/
+ * index.rs:196-234) over the 4-bit polar codes of turbo_quant.rs. */
+
+/* PolarCodec::new + encode_batch (turbo_quant.rs:92-188), as SearchIndex::new builds it
+ * (index.rs:136-158): encodes every stored row under `rotation` (host, [dim, dim] f32 row-major,
+ * rotated_j = sum_d rotation[j][d] x_d; orthogonal in the reference, generate_rotation
+ * turbo_quant.rs:335-343) with `bits` bits per angle (1..4; the reference uses 4).  Per pair of
+ * rotated values: an f32 radius and an angle bin.  The rotation sums in order over d with
+ * rounded products (no fused multiply-add) and the angle is the f64 atan2 rounded to f32, so
+ * codes are reproducible bit for bit.  Rebuilding replaces the previous corpus.  The reference
+ * builds it only for indexes of at least 4096 rows; that policy is the caller's. */
+int rv_index_build_polar(rv_index* idx, const float* rotation, int32_t bits);
+/* 1 when a PolarQuant corpus is present. */
+int rv_index_has_polar(const rv_index* idx);
+/* The corpus in the reference's SoA layout (CompressedCorpus, turbo_quant.rs:39-49): radii
+ * [n, dim/2] f32 and angle bins [n, dim/2] u8, host buffers. */
+int rv_index_polar_export(rv_index* idx, float* radii, uint8_t* bins);
+/* PolarCodec::prepare_query + scan_corpus (turbo_quant.rs:212-289): approximate scores
+ * [nq, n] f32 of the f32 queries [nq, dim] against every row, host buffers. */
+int rv_index_polar_scores(rv_index* idx, const float* queries, int32_t nq, float* scores);
+/* SearchIndex::rank_turboquant (index.rs:196-234) restricted to top_k results: approximate
+ * scores of every row, the best min(10 * top_k, n) rows by (approximate score desc, row asc),
+ * re-scored exactly (as rv_index_topk), rows below threshold dropped, the best top_k by
+ * (score desc, row asc).  Without a corpus it equals rv_index_topk (the reference falls back to
+ * rank, index.rs:202-204).  top_k in [1, 800].  Outputs as rv_index_topk; host buffers. */
+int rv_index_rank_turboquant(rv_index* idx, const float* queries, int32_t nq, int32_t top_k, float threshold,
+                             int64_t* out_idx, float* out_score, double* out_score64, int32_t* out_count);
+/* Device-buffer variant of rv_index_rank_turboquant (outputs as rv_index_topk_device). */
+int rv_index_rank_turboquant_device(rv_index* idx, const float* queries_dev, int32_t nq, int32_t top_k,
+                                    float threshold, int64_t* out_idx_dev, float* out_score_dev,
+                                    double* out_score64_dev, void* stream);
+
 /* ---------------------------------------------------------------- single-kernel entry points
  * Used by the parity tests to check one kernel against the CPU oracle.  Device pointers. */
 /* C[M,N] (f32 or act) = A[M,K] B[N,K]^T with A, B of act dtype (RV_DTYPE_BF16/F16); bn = 128 or

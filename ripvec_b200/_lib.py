@@ -88,6 +88,12 @@ SIGNATURES = {
     "rv_index_topk_device": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_index_topk_noalloc": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_topk_merge_device": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, f32, vp, vp, vp, vp]),
+    "rv_index_build_polar": (C.c_int, [vp, vp, i32]),
+    "rv_index_has_polar": (C.c_int, [vp]),
+    "rv_index_polar_export": (C.c_int, [vp, vp, vp]),
+    "rv_index_polar_scores": (C.c_int, [vp, vp, i32, vp]),
+    "rv_index_rank_turboquant": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
+    "rv_index_rank_turboquant_device": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_op_gemm": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "rv_op_attention": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, f32, vp]),
     "rv_op_layernorm": (C.c_int, [i32, vp, vp, i32, i32, vp, vp, f32, vp]),

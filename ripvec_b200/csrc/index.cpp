@@ -17,6 +17,7 @@
 #include "kernels.h"
 #include "scan.h"
 #include "tmap.h"
+#include "turbo_quant.h"
 
 namespace {
 
@@ -204,6 +205,70 @@ int topk_device(rv_index* x, const float* q_dev, int nq, int k, float threshold,
   }
 }
 
+// SearchIndex::rank_turboquant (index.rs:196-234) over device queries: approximate PolarQuant
+// scores of every row, the best pre = min(10 top_k, n) by (approximate score desc, row asc),
+// exact rescoring of those (the exact path's definition: f64 sums of the bf16 products), rows
+// below the threshold dropped, the best top_k by (score desc, row asc).  Without a compressed
+// corpus it is the exact top-k (the reference falls back to rank, index.rs:202-204).
+constexpr int kTqMaxTopK = 800;  // pre <= 8000 candidates per query
+
+int tq_device(rv_index* x, const float* q_dev, int nq, int top_k, float threshold, int64_t* out_i, float* out_s,
+              double* out_s64, std::vector<int>* counts) {
+  if (nq <= 0) return RV_OK;
+  if (top_k <= 0 || top_k > kTqMaxTopK)
+    return ifail(x, RV_E_INVALID, "top_k must be in [1, " + std::to_string(kTqMaxTopK) + "]");
+  if (x->pq_levels == 0 || x->n == 0)
+    return topk_device(x, q_dev, nq, top_k, threshold, out_i, out_s, out_s64, counts);
+  cudaStream_t st = x->stream;
+  const int dim = x->dim, pairs = dim / 2, levels = x->pq_levels;
+  const int pre = static_cast<int>(std::min<int64_t>(int64_t(10) * top_k, x->n));
+  // Queries per batch: the approximate scores [batch, n] f32 stay under 1 GiB.
+  const int64_t per_q = x->n * 4;
+  const int qg = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(64, (int64_t(1) << 30) / per_q)));
+  const int bq_max = std::min(qg, nq);
+  if (!x->qb.reserve(size_t(bq_max) * dim) || !x->pq_lut.reserve(size_t(bq_max) * pairs * levels) ||
+      !x->pq_s.reserve(size_t(bq_max) * x->n) || !x->pq_state.reserve(size_t(4) * bq_max) ||
+      !x->pq_hist.reserve(size_t(256) * bq_max) || !x->pq_counters.reserve(size_t(2) * bq_max) ||
+      !x->pq_ties.reserve(size_t(bq_max) * rv::polar_tie_cap()) || !x->list_s.reserve(size_t(bq_max) * pre) ||
+      !x->list_i.reserve(size_t(bq_max) * pre) || !x->list_n.reserve(size_t(bq_max)) ||
+      !x->cnt.reserve(size_t(nq)) || !x->guard.reserve(size_t(bq_max)) || !x->overflow.reserve(1))
+    return ifail(x, RV_E_NOMEM, "turboquant scratch allocation failed");
+  IX_TRY(x, cudaMemsetAsync(x->overflow.p, 0, sizeof(int), st));
+  for (int b0 = 0; b0 < nq; b0 += bq_max) {
+    const int bq = std::min(bq_max, nq - b0);
+    const float* qd = q_dev + size_t(b0) * dim;
+    IX_TRY(x, rv::scan_round_queries(qd, x->qb.p, int64_t(bq) * dim, st));
+    IX_TRY(x, rv::polar_query_tables(qd, bq, dim, x->pq_rt.p, x->pq_cs.p, levels, x->pq_lut.p, st));
+    IX_TRY(x, rv::polar_scan(x->pq_radii.p, x->pq_bins.p, pairs, 0, x->n, x->pq_lut.p, bq, levels, x->pq_s.p,
+                             x->n, st));
+    IX_TRY(x, rv::polar_select(x->pq_s.p, x->n, x->n, x->base, bq, pre, x->pq_state.p, x->pq_hist.p,
+                               x->pq_counters.p, x->pq_ties.p, x->list_i.p, x->list_n.p, x->overflow.p, st));
+    const size_t o = size_t(b0) * top_k;
+    IX_TRY(x, rv::scan_rescore(x->db, x->base, dim, x->qb.p, bq, x->list_s.p, x->list_i.p, x->list_n.p, pre,
+                               top_k, x->n, 0.0, threshold, out_i + o, out_s + o,
+                               out_s64 ? out_s64 + o : nullptr, x->cnt.p + b0, x->guard.p, st));
+    x->launches += 13;
+  }
+  int ovf = 0;
+  unsigned int e = 0;
+  IX_TRY(x, cudaMemcpyAsync(&ovf, x->overflow.p, sizeof(int), cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaMemcpyAsync(&e, x->d_err, 4, cudaMemcpyDeviceToHost, st));
+  if (counts) {
+    counts->resize(nq);
+    IX_TRY(x, cudaMemcpyAsync(counts->data(), x->cnt.p, sizeof(int) * nq, cudaMemcpyDeviceToHost, st));
+  }
+  IX_TRY(x, cudaStreamSynchronize(st));
+  if (e) {
+    cudaMemset(x->d_err, 0, 4);
+    return ifail(x, RV_E_DEVICE, "turboquant kernel reported device error flags " + std::to_string(e));
+  }
+  if (ovf)
+    return ifail(x, RV_E_DEVICE,
+                 "turboquant: more than " + std::to_string(rv::polar_tie_cap()) +
+                     " rows share the approximate score at the pre-filter boundary");
+  return RV_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -301,6 +366,23 @@ void rv_index_destroy(rv_index* x) {
     x->cnt.release();
     x->guard.release();
     x->os64.release();
+    x->thr.release();
+    x->cand_s.release();
+    x->cand_i.release();
+    x->cand_n.release();
+    x->overflow.release();
+    x->rec_n.release();
+    x->rec.release();
+    x->pq_radii.release();
+    x->pq_rt.release();
+    x->pq_cs.release();
+    x->pq_lut.release();
+    x->pq_s.release();
+    x->pq_bins.release();
+    x->pq_state.release();
+    x->pq_hist.release();
+    x->pq_counters.release();
+    x->pq_ties.release();
     if (x->stream) cudaStreamDestroy(x->stream);
   }
   delete x;
@@ -382,6 +464,149 @@ int rv_topk_merge_device(int device, const int64_t* idx_in, const double* score_
       cudaSuccess)
     return RV_E_CUDA;
   return cudaStreamSynchronize(st) == cudaSuccess ? RV_OK : RV_E_CUDA;
+}
+
+int rv_index_build_polar(rv_index* x, const float* rotation, int32_t bits) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (!rotation) return ifail(x, RV_E_INVALID, "null rotation");
+  if (bits < 1 || bits > 4) return ifail(x, RV_E_INVALID, "bits must be in [1, 4]");
+  if (x->n <= 0) return ifail(x, RV_E_INVALID, "empty index");
+  const int dim = x->dim, pairs = dim / 2, levels = 1 << bits;
+  if (size_t(pairs) * levels * sizeof(float) > rv::kPolarMaxLutBytes)
+    return ifail(x, RV_E_INVALID, "dimension too large for the PolarQuant query tables");
+  Dev g(x->device);
+  cudaStream_t st = x->stream;
+  // rt[d * dim + j] = R[j][d]: the encode and table kernels read a column of R per dimension.
+  std::vector<float> rt(size_t(dim) * dim);
+  for (int j = 0; j < dim; ++j)
+    for (int d = 0; d < dim; ++d) rt[size_t(d) * dim + j] = rotation[size_t(j) * dim + d];
+  // theta_j = (j / levels) * 2 * PI - PI in f32 (turbo_quant.rs:104-109); cos / sin from the f64
+  // functions rounded to f32.
+  std::vector<float> cs(size_t(2) * levels);
+  const float pi_f = 3.14159265358979323846f;
+  for (int j = 0; j < levels; ++j) {
+    volatile float t = static_cast<float>(j) / static_cast<float>(levels);
+    t = t * 2.0f;
+    t = t * pi_f;
+    t = t - pi_f;
+    cs[j] = static_cast<float>(std::cos(static_cast<double>(t)));
+    cs[levels + j] = static_cast<float>(std::sin(static_cast<double>(t)));
+  }
+  const size_t rows_padded = size_t((x->n + 31) / 32) * 32;
+  if (!x->pq_rt.reserve(rt.size()) || !x->pq_cs.reserve(cs.size()) ||
+      !x->pq_radii.reserve(rows_padded * pairs) || !x->pq_bins.reserve(rows_padded * pairs))
+    return ifail(x, RV_E_NOMEM, "PolarQuant corpus allocation failed");
+  IX_TRY(x, cudaMemcpyAsync(x->pq_rt.p, rt.data(), rt.size() * sizeof(float), cudaMemcpyHostToDevice, st));
+  IX_TRY(x, cudaMemcpyAsync(x->pq_cs.p, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice, st));
+  IX_TRY(x, cudaMemsetAsync(x->pq_radii.p, 0, rows_padded * pairs * sizeof(float), st));
+  IX_TRY(x, cudaMemsetAsync(x->pq_bins.p, 0, rows_padded * pairs, st));
+  IX_TRY(x, rv::polar_encode(x->db, x->n, dim, x->pq_rt.p, levels, x->pq_radii.p, x->pq_bins.p, st));
+  x->launches++;
+  IX_TRY(x, cudaStreamSynchronize(st));
+  x->pq_levels = levels;
+  return RV_OK;
+}
+
+int rv_index_has_polar(const rv_index* x) { return x && x->pq_levels ? 1 : 0; }
+
+int rv_index_polar_export(rv_index* x, float* radii, uint8_t* bins) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (!x->pq_levels) return ifail(x, RV_E_NOT_READY, "no PolarQuant corpus");
+  if (!radii || !bins) return ifail(x, RV_E_INVALID, "null argument");
+  Dev g(x->device);
+  const int pairs = x->dim / 2;
+  const size_t rows_padded = size_t((x->n + 31) / 32) * 32;
+  std::vector<float> r(rows_padded * pairs);
+  std::vector<uint8_t> b(rows_padded * pairs);
+  IX_TRY(x, cudaMemcpyAsync(r.data(), x->pq_radii.p, r.size() * sizeof(float), cudaMemcpyDeviceToHost, x->stream));
+  IX_TRY(x, cudaMemcpyAsync(b.data(), x->pq_bins.p, b.size(), cudaMemcpyDeviceToHost, x->stream));
+  IX_TRY(x, cudaStreamSynchronize(x->stream));
+  for (int64_t row = 0; row < x->n; ++row) {
+    const int64_t grp = row / 32;
+    const int lane = static_cast<int>(row % 32);
+    for (int p = 0; p < pairs; ++p) {
+      radii[size_t(row) * pairs + p] = r[((size_t(grp) * (pairs / 4) + p / 4) * 32 + lane) * 4 + (p % 4)];
+      bins[size_t(row) * pairs + p] = b[((size_t(grp) * (pairs / 16) + p / 16) * 32 + lane) * 16 + (p % 16)];
+    }
+  }
+  return RV_OK;
+}
+
+int rv_index_polar_scores(rv_index* x, const float* queries, int32_t nq, float* scores) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (!x->pq_levels) return ifail(x, RV_E_NOT_READY, "no PolarQuant corpus");
+  if (nq < 0 || (nq > 0 && (!queries || !scores))) return ifail(x, RV_E_INVALID, "null argument");
+  if (nq == 0) return RV_OK;
+  Dev g(x->device);
+  cudaStream_t st = x->stream;
+  const int dim = x->dim, pairs = dim / 2, levels = x->pq_levels;
+  if (!x->qf.reserve(size_t(nq) * dim) || !x->pq_lut.reserve(size_t(nq) * pairs * levels) ||
+      !x->pq_s.reserve(size_t(nq) * x->n))
+    return ifail(x, RV_E_NOMEM, "PolarQuant score buffers");
+  IX_TRY(x, cudaMemcpyAsync(x->qf.p, queries, sizeof(float) * size_t(nq) * dim, cudaMemcpyHostToDevice, st));
+  IX_TRY(x, rv::polar_query_tables(x->qf.p, nq, dim, x->pq_rt.p, x->pq_cs.p, levels, x->pq_lut.p, st));
+  IX_TRY(x, rv::polar_scan(x->pq_radii.p, x->pq_bins.p, pairs, 0, x->n, x->pq_lut.p, nq, levels, x->pq_s.p, x->n,
+                           st));
+  IX_TRY(x, cudaMemcpyAsync(scores, x->pq_s.p, sizeof(float) * size_t(nq) * x->n, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaStreamSynchronize(st));
+  return RV_OK;
+}
+
+int rv_index_rank_turboquant_device(rv_index* x, const float* q_dev, int32_t nq, int32_t top_k, float threshold,
+                                    int64_t* out_i, float* out_s, double* out_s64, void* stream) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (nq < 0 || (nq > 0 && (!q_dev || !out_i || !out_s))) return ifail(x, RV_E_INVALID, "null argument");
+  Dev g(x->device);
+  cudaStream_t user = static_cast<cudaStream_t>(stream);
+  cudaEvent_t ev = nullptr;
+  if (user) {
+    IX_TRY(x, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    IX_TRY(x, cudaEventRecord(ev, user));
+    IX_TRY(x, cudaStreamWaitEvent(x->stream, ev, 0));
+  }
+  int rc = tq_device(x, q_dev, nq, top_k, threshold, out_i, out_s, out_s64, nullptr);
+  if (ev) {
+    if (rc == RV_OK) {
+      cudaEventRecord(ev, x->stream);
+      cudaStreamWaitEvent(user, ev, 0);
+    }
+    cudaEventDestroy(ev);
+  }
+  return rc;
+}
+
+int rv_index_rank_turboquant(rv_index* x, const float* queries, int32_t nq, int32_t top_k, float threshold,
+                             int64_t* out_idx, float* out_score, double* out_score64, int32_t* out_count) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (nq < 0 || (nq > 0 && (!queries || !out_idx || !out_score)))
+    return ifail(x, RV_E_INVALID, "null argument");
+  if (nq == 0) return RV_OK;
+  if (top_k <= 0 || top_k > kTqMaxTopK)
+    return ifail(x, RV_E_INVALID, "top_k must be in [1, " + std::to_string(kTqMaxTopK) + "]");
+  Dev g(x->device);
+  cudaStream_t st = x->stream;
+  const size_t nk = size_t(nq) * top_k;
+  if (!x->qf.reserve(size_t(nq) * x->dim) || !x->oi.reserve(nk) || !x->os.reserve(nk) ||
+      (out_score64 && !x->os64.reserve(nk)))
+    return ifail(x, RV_E_NOMEM, "turboquant buffers");
+  IX_TRY(x, cudaMemcpyAsync(x->qf.p, queries, sizeof(float) * size_t(nq) * x->dim, cudaMemcpyHostToDevice, st));
+  std::vector<int> counts;
+  int rc = tq_device(x, x->qf.p, nq, top_k, threshold, x->oi.p, x->os.p, out_score64 ? x->os64.p : nullptr,
+                     &counts);
+  if (rc) return rc;
+  IX_TRY(x, cudaMemcpyAsync(out_idx, x->oi.p, sizeof(int64_t) * nk, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaMemcpyAsync(out_score, x->os.p, sizeof(float) * nk, cudaMemcpyDeviceToHost, st));
+  if (out_score64)
+    IX_TRY(x, cudaMemcpyAsync(out_score64, x->os64.p, sizeof(double) * nk, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaStreamSynchronize(st));
+  if (out_count)
+    for (int q = 0; q < nq; ++q) out_count[q] = counts[q];
+  return RV_OK;
 }
 
 }  // extern "C"

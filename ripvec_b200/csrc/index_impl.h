@@ -52,6 +52,14 @@ struct rv_index {
   DevBuf<int64_t> cand_i;
   DevBuf<int> cand_n, overflow, rec_n;
   DevBuf<int4> rec;
+  // PolarQuant ("TurboQuant") corpus (turbo_quant.cu), built by rv_index_build_polar:
+  // interleaved radii / angle bins, the transposed rotation, the cos / sin tables, and the
+  // per-call query tables, approximate scores and selection scratch.
+  int pq_levels = 0;  // 0: no compressed corpus
+  DevBuf<float> pq_radii, pq_rt, pq_cs, pq_lut, pq_s;
+  DevBuf<uint8_t> pq_bins;
+  DevBuf<uint32_t> pq_state, pq_hist, pq_counters;
+  DevBuf<int64_t> pq_ties;
   int64_t launches = 0;
   bool filter_off = false;  // RV_SCAN_FILTER=0 at creation
 };

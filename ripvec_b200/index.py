@@ -7,6 +7,9 @@ gives no results, rows scoring below ``threshold`` are dropped, results are sort
 score.  Differences, by design: rows are stored in bf16 and queries are rounded to bf16, scores
 are exact sums of the bf16 products (so equal inputs give bit-identical rankings), ties are
 ordered by row index, and one call returns at most 2048 rows per query (``top_k``).
+
+``rank_turboquant`` mirrors ``SearchIndex::rank_turboquant`` (``index.rs:196-234``) over the
+PolarQuant codes of ``turbo_quant.rs``, built on the GPU by ``build_turboquant``.
 """
 
 from __future__ import annotations
@@ -18,10 +21,39 @@ import numpy as np
 from . import _lib as L
 
 MAX_K = 2048
+TURBOQUANT_MIN_CHUNKS = 4096  # index.rs:22
+TURBOQUANT_MAX_TOP_K = 800
+
+
+def turboquant_eligible(n: int, dim: int) -> bool:
+    """``SearchIndex::new`` builds the compressed corpus only for at least 4096 rows of an even
+    dimension of at least 64 (``index.rs:136-140``)."""
+    return n >= TURBOQUANT_MIN_CHUNKS and dim >= 64 and dim % 2 == 0
+
+
+def polar_rotation(dim: int, seed: int = 42) -> np.ndarray:
+    """A seeded orthogonal [dim, dim] f32 rotation: modified Gram-Schmidt over the columns of a
+    standard-normal matrix, as ``generate_rotation`` / ``gram_schmidt_qr`` do
+    (``turbo_quant.rs:335-367``).  The normal samples come from numpy's generator, so the matrix
+    is not the reference's ChaCha8-seeded one; pass that matrix to ``build_turboquant`` to get
+    the reference's codes."""
+    q = np.random.default_rng(seed).standard_normal((dim, dim)).astype(np.float32)
+    for i in range(dim):
+        norm = np.float32(np.sqrt(np.sum(q[:, i] * q[:, i], dtype=np.float32)))
+        if norm < 1e-10:
+            continue
+        q[:, i] *= np.float32(1.0) / norm
+        if i + 1 < dim:
+            q[:, i + 1:] -= (q[:, i][None, :] @ q[:, i + 1:]).astype(np.float32) * q[:, i][:, None]
+    return q
 
 
 class SearchIndex:
-    def __init__(self, embeddings, device: int = 0, base: int = 0):
+    def __init__(self, embeddings, device: int = 0, base: int = 0, turboquant: bool | str = False,
+                 turboquant_seed: int = 42):
+        """``turboquant``: ``False`` (default) keeps only the exact index; ``"auto"`` builds the
+        PolarQuant corpus when ``SearchIndex::new`` would (``turboquant_eligible``); ``True``
+        builds it for any size."""
         self._lib = L.lib()
         h = C.c_void_p()
         if hasattr(embeddings, "data_ptr"):  # device tensor (torch): f32 or bf16
@@ -45,6 +77,8 @@ class SearchIndex:
         self.device = device
         if base:
             self._check(self._lib.rv_index_set_base(self._h, base))
+        if turboquant is True or (turboquant == "auto" and turboquant_eligible(int(n), int(dim))):
+            self.build_turboquant(polar_rotation(int(dim), turboquant_seed))
 
     def _check(self, rc: int) -> None:
         if rc != L.RV_OK:
@@ -98,6 +132,66 @@ class SearchIndex:
         if k <= 0:
             return []
         oi, os_, cnt = self.topk(q[None, :], k, threshold)
+        return [(int(oi[0, i]), float(os_[0, i])) for i in range(int(cnt[0]))]
+
+    # ------------------------------------------------------------ PolarQuant ("TurboQuant")
+    def build_turboquant(self, rotation: np.ndarray, bits: int = 4) -> None:
+        """``PolarCodec::new`` + ``encode_batch`` of the stored rows under ``rotation``."""
+        r = np.ascontiguousarray(rotation, np.float32)
+        if r.shape != (self.hidden_dim, self.hidden_dim):
+            raise ValueError(f"rotation must be [{self.hidden_dim}, {self.hidden_dim}]")
+        self._check(self._lib.rv_index_build_polar(self._h, r.ctypes.data, bits))
+
+    @property
+    def has_turboquant(self) -> bool:
+        return bool(self._lib.rv_index_has_polar(self._h))
+
+    def turboquant_codes(self) -> tuple[np.ndarray, np.ndarray]:
+        """The compressed corpus as ``(radii f32 [n, dim/2], bins u8 [n, dim/2])``."""
+        n, pairs = len(self), self.hidden_dim // 2
+        radii = np.empty((n, pairs), np.float32)
+        bins = np.empty((n, pairs), np.uint8)
+        self._check(self._lib.rv_index_polar_export(self._h, radii.ctypes.data, bins.ctypes.data))
+        return radii, bins
+
+    def turboquant_scores(self, queries) -> np.ndarray:
+        """``scan_corpus`` of each query: approximate scores ``[nq, n]`` f32."""
+        q = np.ascontiguousarray(queries, np.float32).reshape(-1, self.hidden_dim)
+        out = np.empty((q.shape[0], len(self)), np.float32)
+        self._check(self._lib.rv_index_polar_scores(self._h, q.ctypes.data, q.shape[0], out.ctypes.data))
+        return out
+
+    def topk_turboquant(self, queries, top_k: int, threshold: float = float("-inf"), with_f64: bool = False):
+        """``rank_turboquant`` for a batch of queries, as arrays like ``topk``."""
+        q = np.ascontiguousarray(queries, np.float32).reshape(-1, self.hidden_dim)
+        nq = q.shape[0]
+        oi = np.empty((nq, top_k), np.int64)
+        os_ = np.empty((nq, top_k), np.float32)
+        o64 = np.empty((nq, top_k), np.float64) if with_f64 else None
+        cnt = np.empty(nq, np.int32)
+        self._check(self._lib.rv_index_rank_turboquant(self._h, q.ctypes.data, nq, top_k, threshold, oi.ctypes.data,
+                                                       os_.ctypes.data, o64.ctypes.data if with_f64 else None,
+                                                       cnt.ctypes.data))
+        return (oi, os_, cnt, o64) if with_f64 else (oi, os_, cnt)
+
+    def topk_turboquant_device(self, queries_dev, top_k: int, out_idx, out_score, out_score64=None,
+                               threshold: float = float("-inf"), stream: int = 0) -> None:
+        nq = queries_dev.shape[0]
+        self._check(self._lib.rv_index_rank_turboquant_device(self._h, L.ptr(queries_dev), nq, top_k, threshold,
+                                                              L.ptr(out_idx), L.ptr(out_score),
+                                                              L.ptr(out_score64), stream or None))
+
+    def rank_turboquant(self, query, top_k: int, threshold: float) -> list[tuple[int, float]]:
+        """``SearchIndex::rank_turboquant`` (``index.rs:196-234``): ``(row, score)`` pairs, at
+        most ``top_k``, sorted by descending exact score.  A query of the wrong dimension is an
+        error (the reference's ``prepare_query`` asserts the length)."""
+        q = np.asarray(query, np.float32).reshape(-1)
+        if q.shape[0] != self.hidden_dim:
+            raise ValueError(f"query has {q.shape[0]} dimensions, the index {self.hidden_dim}")
+        n = len(self)
+        if n == 0 or top_k <= 0:
+            return []
+        oi, os_, cnt = self.topk_turboquant(q[None, :], min(top_k, TURBOQUANT_MAX_TOP_K), threshold)
         return [(int(oi[0, i]), float(os_[0, i])) for i in range(int(cnt[0]))]
 
 
