@@ -196,6 +196,25 @@ int rv_index_rank_turboquant_device(rv_index* idx, const float* queries_dev, int
                                     float threshold, int64_t* out_idx_dev, float* out_score_dev,
                                     double* out_score64_dev, void* stream);
 
+/* ---------------------------------------------------------------- MRL cascade search */
+/* SearchIndex::new with cascade_dim (crates/ripvec-core/src/index.rs:99-132): builds the
+ * truncated matrix of the stored rows: LayerNorm over the full row (mean, biased variance,
+ * 1 / sqrt(var + 1e-5)), the first trunc_dim values, L2-normalised (norm floored at 1e-12); sums
+ * in order over the dimensions in f32, stored in bf16.  trunc_dim is clamped to the row
+ * dimension and must then be a multiple of 64.  Rebuilding replaces the previous matrix. */
+int rv_index_build_cascade(rv_index* idx, int32_t trunc_dim);
+/* The truncated dimension, or 0 without a truncated matrix (SearchIndex::truncated_dim). */
+int rv_index_cascade_dim(const rv_index* idx);
+/* The truncated matrix [n, trunc_dim] as f32 (the stored bf16 values), host buffer. */
+int rv_index_cascade_rows(rv_index* idx, float* out);
+/* SearchIndex::rank_cascade (index.rs:245-297): the query gets the same transform; the best
+ * max(100, 3 top_k) rows of the truncated matrix (exact top-k there) are re-scored exactly
+ * with the full rows (as rv_index_topk), rows below threshold dropped, the best top_k by
+ * (score desc, row asc).  Without a truncated matrix it equals rv_index_topk (the reference
+ * falls back to rank).  top_k in [1, 682].  Outputs as rv_index_topk; host buffers. */
+int rv_index_rank_cascade(rv_index* idx, const float* queries, int32_t nq, int32_t top_k, float threshold,
+                          int64_t* out_idx, float* out_score, double* out_score64, int32_t* out_count);
+
 /* ---------------------------------------------------------------- single-kernel entry points
  * Used by the parity tests to check one kernel against the CPU oracle.  Device pointers. */
 /* C[M,N] (f32 or act) = A[M,K] B[N,K]^T with A, B of act dtype (RV_DTYPE_BF16/F16); bn = 128 or

@@ -8,6 +8,8 @@ check (wrong or empty query -> no results), scores ``embeddings @ query`` (``sim
 leaves the order of equal scores unspecified; this build fixes it to (score desc, row asc), the
 order ``rrf_fuse`` uses (``hybrid.rs:198-200``).
 
+``ln_truncate`` / ``rank_cascade`` restate the MRL cascade (``index.rs:99-132``, ``:245-297``).
+
 ``topk_exact`` is the bit-exact definition the GPU scan is checked against: rows and query are
 bf16 values, each score is the sequential sum over d = 0..dim-1 in float64 of the (exact)
 bf16 x bf16 products, results are ordered by (score desc, row asc), the best k are kept, and
@@ -100,6 +102,58 @@ def topk_exact(db: np.ndarray, queries: np.ndarray, k: int, threshold: float = -
         out_s[qi, :c] = best_s[qi][sel]
         cnt[qi] = c
     return out_i, out_s, cnt
+
+
+def ln_truncate(x: np.ndarray, t: int) -> np.ndarray:
+    """MRL cascade transform of ``SearchIndex::new`` (``index.rs:99-132``) and of the query in
+    ``rank_cascade`` (``index.rs:262-283``): LayerNorm over the full vector (mean, biased
+    variance, ``1 / sqrt(var + 1e-5)``), the first ``t`` values, divided by their L2 norm floored
+    at 1e-12.  Every sum runs over the dimensions in order in f32 (``iter().sum()``)."""
+    x = np.asarray(x, np.float32)
+    m, dim = x.shape
+    t = min(t, dim)
+    s = np.zeros(m, np.float32)
+    for d in range(dim):
+        s += x[:, d]
+    mean = (s / np.float32(dim)).astype(np.float32)
+    v = np.zeros(m, np.float32)
+    for d in range(dim):
+        c = (x[:, d] - mean).astype(np.float32)
+        v += c * c
+    var = (v / np.float32(dim)).astype(np.float32)
+    inv = (np.float32(1.0) / np.sqrt(var + np.float32(1e-5))).astype(np.float32)
+    nn = np.zeros(m, np.float32)
+    for j in range(t):
+        ln = ((x[:, j] - mean) * inv).astype(np.float32)
+        nn += ln * ln
+    norm = np.maximum(np.sqrt(nn), np.float32(1e-12)).astype(np.float32)
+    ln = ((x[:, :t] - mean[:, None]) * inv[:, None]).astype(np.float32)
+    return (ln / norm[:, None]).astype(np.float32)
+
+
+def rank_cascade(rows: np.ndarray, query, top_k: int, threshold: float, cascade_dim: int | None):
+    """``SearchIndex::rank_cascade`` (``index.rs:245-297``) for one query: ``(idx int64 [m],
+    score f64 [m])``, m <= top_k.  Phase 1 is the exact top ``max(100, 3 top_k)`` of the
+    truncated rows (stored in bf16) against the truncated query; phase 2 re-scores those rows
+    with the full rows (``scores_exact``), keeps ``score >= threshold`` and the best ``top_k`` by
+    (score desc, row asc).  ``cascade_dim=None``: no truncated matrix, the exact top-k (the
+    reference's ``rank`` fallback, truncated by its callers)."""
+    rows = np.asarray(rows, np.float32)
+    q = np.asarray(query, np.float32).reshape(1, -1)
+    if cascade_dim is None:
+        ei, es, ec = topk_exact(rows, q, top_k, threshold)
+        return ei[0, :ec[0]], es[0, :ec[0]]
+    rb = ops.to_bf16(rows)
+    tr = ops.to_bf16(ln_truncate(rb, cascade_dim))
+    tq = ln_truncate(q, cascade_dim)
+    pre = max(100, 3 * top_k)
+    ci, _, cc = topk_exact(tr, tq, pre)
+    cand = ci[0, :cc[0]]
+    exact = scores_exact(rb[cand], ops.to_bf16(q[0]))
+    keep = exact >= threshold
+    cand, exact = cand[keep], exact[keep]
+    order = np.lexsort((cand, -exact))[:top_k]
+    return cand[order].astype(np.int64), exact[order]
 
 
 def merge_topk(idx_lists: np.ndarray, score_lists: np.ndarray, k: int, threshold: float = -np.inf):

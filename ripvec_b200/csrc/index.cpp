@@ -13,6 +13,7 @@
 
 #include "../../include/ripvec_b200.h"
 #include "engine.h"
+#include "cascade.h"
 #include "index_impl.h"
 #include "kernels.h"
 #include "scan.h"
@@ -350,6 +351,8 @@ int rv_index_create(int device, const void* src, int64_t n, int32_t dim, int32_t
 
 void rv_index_destroy(rv_index* x) {
   if (!x) return;
+  rv_index_destroy(x->cascade);
+  x->cascade = nullptr;
   {
     Dev g(x->device);
     if (x->stream) cudaStreamSynchronize(x->stream);
@@ -383,6 +386,9 @@ void rv_index_destroy(rv_index* x) {
     x->pq_hist.release();
     x->pq_counters.release();
     x->pq_ties.release();
+    x->c_q.release();
+    x->c_os.release();
+    x->c_oi.release();
     if (x->stream) cudaStreamDestroy(x->stream);
   }
   delete x;
@@ -606,6 +612,112 @@ int rv_index_rank_turboquant(rv_index* x, const float* queries, int32_t nq, int3
   IX_TRY(x, cudaStreamSynchronize(st));
   if (out_count)
     for (int q = 0; q < nq; ++q) out_count[q] = counts[q];
+  return RV_OK;
+}
+
+int rv_index_build_cascade(rv_index* x, int32_t trunc_dim) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (x->n <= 0) return ifail(x, RV_E_INVALID, "empty index");
+  const int t = std::min<int>(trunc_dim, x->dim);  // index.rs:99 clamps to hidden_dim
+  if (t <= 0 || t % 64 != 0) return ifail(x, RV_E_INVALID, "truncated dimension must be a positive multiple of 64");
+  if (rv::cascade_rows_smem(x->dim, t) > rv::kCascadeMaxSmem)
+    return ifail(x, RV_E_INVALID, "dimension too large for the cascade transform");
+  Dev g(x->device);
+  __nv_bfloat16* tmp = nullptr;
+  IX_TRY(x, cudaMalloc(&tmp, size_t(x->n) * t * 2));
+  cudaError_t e = rv::cascade_rows(x->db, x->n, x->dim, t, tmp, x->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(x->stream);
+  if (e != cudaSuccess) {
+    cudaFree(tmp);
+    return ifail(x, RV_E_CUDA, std::string("cascade_rows: ") + cudaGetErrorString(e));
+  }
+  x->launches++;
+  rv_index* c = nullptr;
+  const int rc = rv_index_create(x->device, tmp, x->n, t, RV_DTYPE_BF16, 1, &c);
+  cudaFree(tmp);
+  if (rc != RV_OK) return ifail(x, rc, "truncated index creation failed");
+  rv_index_destroy(x->cascade);
+  x->cascade = c;
+  return RV_OK;
+}
+
+int rv_index_cascade_dim(const rv_index* x) { return x && x->cascade ? x->cascade->dim : 0; }
+
+int rv_index_rank_cascade(rv_index* x, const float* queries, int32_t nq, int32_t top_k, float threshold,
+                          int64_t* out_idx, float* out_score, double* out_score64, int32_t* out_count) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (nq < 0 || (nq > 0 && (!queries || !out_idx || !out_score)))
+    return ifail(x, RV_E_INVALID, "null argument");
+  if (nq == 0) return RV_OK;
+  // pre_filter_k = max(100, 3 top_k) (index.rs:261) must fit one exact top-k call (<= 2048).
+  if (top_k <= 0 || top_k > 682) return ifail(x, RV_E_INVALID, "top_k must be in [1, 682]");
+  Dev g(x->device);
+  cudaStream_t st = x->stream;
+  const size_t nk = size_t(nq) * top_k;
+  if (!x->qf.reserve(size_t(nq) * x->dim) || !x->oi.reserve(nk) || !x->os.reserve(nk) ||
+      (out_score64 && !x->os64.reserve(nk)))
+    return ifail(x, RV_E_NOMEM, "cascade buffers");
+  IX_TRY(x, cudaMemcpyAsync(x->qf.p, queries, sizeof(float) * size_t(nq) * x->dim, cudaMemcpyHostToDevice, st));
+  std::vector<int> counts;
+  int rc;
+  if (!x->cascade || x->n == 0) {
+    // No truncated matrix: the exact ranking (index.rs:252-254 falls back to rank).
+    rc = topk_device(x, x->qf.p, nq, top_k, threshold, x->oi.p, x->os.p, out_score64 ? x->os64.p : nullptr,
+                     &counts);
+  } else {
+    rv_index* c = x->cascade;
+    const int t = c->dim;
+    const int pre = std::max(100, 3 * top_k);
+    if (!x->c_q.reserve(size_t(nq) * t) || !x->c_oi.reserve(size_t(nq) * pre) || !x->c_os.reserve(size_t(nq) * pre) ||
+        !x->qb.reserve(size_t(nq) * x->dim) || !x->cnt.reserve(size_t(nq)) || !x->guard.reserve(size_t(nq)))
+      return ifail(x, RV_E_NOMEM, "cascade buffers");
+    // Phase 1: exact top-pre of the truncated queries over the truncated rows.
+    IX_TRY(x, rv::cascade_queries(x->qf.p, nq, x->dim, t, x->c_q.p, st));
+    IX_TRY(x, cudaStreamSynchronize(st));
+    {
+      std::lock_guard<std::mutex> lc(c->mu);
+      c->base = x->base;
+      rc = topk_device(c, x->c_q.p, nq, pre, -INFINITY, x->c_oi.p, x->c_os.p, nullptr, nullptr);
+      if (rc) return ifail(x, rc, "cascade first phase: " + c->err);
+      // Phase 2: exact rescoring of the candidates with the full rows (index.rs:287-296).
+      // topk_device returned after synchronising c's stream; its counts are in c->cnt.
+      IX_TRY(x, rv::scan_round_queries(x->qf.p, x->qb.p, int64_t(nq) * x->dim, st));
+      IX_TRY(x, rv::scan_rescore(x->db, x->base, x->dim, x->qb.p, nq, x->c_os.p, x->c_oi.p, c->cnt.p, pre, top_k,
+                                 x->n, 0.0, threshold, x->oi.p, x->os.p, out_score64 ? x->os64.p : nullptr,
+                                 x->cnt.p, x->guard.p, st));
+      x->launches += 3;
+      counts.resize(nq);
+      IX_TRY(x, cudaMemcpyAsync(counts.data(), x->cnt.p, sizeof(int) * nq, cudaMemcpyDeviceToHost, st));
+      IX_TRY(x, cudaStreamSynchronize(st));
+    }
+    rc = RV_OK;
+  }
+  if (rc) return rc;
+  IX_TRY(x, cudaMemcpyAsync(out_idx, x->oi.p, sizeof(int64_t) * nk, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaMemcpyAsync(out_score, x->os.p, sizeof(float) * nk, cudaMemcpyDeviceToHost, st));
+  if (out_score64)
+    IX_TRY(x, cudaMemcpyAsync(out_score64, x->os64.p, sizeof(double) * nk, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaStreamSynchronize(st));
+  if (out_count)
+    for (int q = 0; q < nq; ++q) out_count[q] = counts[q];
+  return RV_OK;
+}
+
+int rv_index_cascade_rows(rv_index* x, float* out) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (!x->cascade) return ifail(x, RV_E_NOT_READY, "no truncated matrix");
+  if (!out) return ifail(x, RV_E_INVALID, "null argument");
+  Dev g(x->device);
+  const size_t m = size_t(x->n) * x->cascade->dim;
+  std::vector<uint16_t> h(m);
+  IX_TRY(x, cudaMemcpy(h.data(), x->cascade->db, m * 2, cudaMemcpyDeviceToHost));
+  for (size_t i = 0; i < m; ++i) {
+    const uint32_t u = uint32_t(h[i]) << 16;
+    std::memcpy(out + i, &u, 4);
+  }
   return RV_OK;
 }
 

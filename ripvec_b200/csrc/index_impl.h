@@ -60,6 +60,11 @@ struct rv_index {
   DevBuf<uint8_t> pq_bins;
   DevBuf<uint32_t> pq_state, pq_hist, pq_counters;
   DevBuf<int64_t> pq_ties;
+  // MRL cascade (cascade.cu): an index over the truncated, re-normalised rows, built by
+  // rv_index_build_cascade, and the per-call truncated queries and first-phase candidates.
+  rv_index* cascade = nullptr;
+  DevBuf<float> c_q, c_os;
+  DevBuf<int64_t> c_oi;
   int64_t launches = 0;
   bool filter_off = false;  // RV_SCAN_FILTER=0 at creation
 };

@@ -50,10 +50,11 @@ def polar_rotation(dim: int, seed: int = 42) -> np.ndarray:
 
 class SearchIndex:
     def __init__(self, embeddings, device: int = 0, base: int = 0, turboquant: bool | str = False,
-                 turboquant_seed: int = 42):
+                 turboquant_seed: int = 42, cascade_dim: int | None = None):
         """``turboquant``: ``False`` (default) keeps only the exact index; ``"auto"`` builds the
         PolarQuant corpus when ``SearchIndex::new`` would (``turboquant_eligible``); ``True``
-        builds it for any size."""
+        builds it for any size.  ``cascade_dim``: builds the truncated matrix of the MRL cascade
+        (``SearchIndex::new``'s ``cascade_dim``, clamped to the row dimension)."""
         self._lib = L.lib()
         h = C.c_void_p()
         if hasattr(embeddings, "data_ptr"):  # device tensor (torch): f32 or bf16
@@ -79,6 +80,8 @@ class SearchIndex:
             self._check(self._lib.rv_index_set_base(self._h, base))
         if turboquant is True or (turboquant == "auto" and turboquant_eligible(int(n), int(dim))):
             self.build_turboquant(polar_rotation(int(dim), turboquant_seed))
+        if cascade_dim is not None:
+            self._check(self._lib.rv_index_build_cascade(self._h, cascade_dim))
 
     def _check(self, rc: int) -> None:
         if rc != L.RV_OK:
@@ -192,6 +195,41 @@ class SearchIndex:
         if n == 0 or top_k <= 0:
             return []
         oi, os_, cnt = self.topk_turboquant(q[None, :], min(top_k, TURBOQUANT_MAX_TOP_K), threshold)
+        return [(int(oi[0, i]), float(os_[0, i])) for i in range(int(cnt[0]))]
+
+
+    # ------------------------------------------------------------ MRL cascade
+    def truncated_dim(self) -> int | None:
+        """``SearchIndex::truncated_dim``."""
+        t = int(self._lib.rv_index_cascade_dim(self._h))
+        return t or None
+
+    def truncated_rows(self) -> np.ndarray:
+        """The truncated, re-normalised matrix ``[n, truncated_dim]`` (bf16 values as f32)."""
+        out = np.empty((len(self), self.truncated_dim() or 0), np.float32)
+        self._check(self._lib.rv_index_cascade_rows(self._h, out.ctypes.data))
+        return out
+
+    def topk_cascade(self, queries, top_k: int, threshold: float = float("-inf"), with_f64: bool = False):
+        """``rank_cascade`` for a batch of queries, as arrays like ``topk``."""
+        q = np.ascontiguousarray(queries, np.float32).reshape(-1, self.hidden_dim)
+        nq = q.shape[0]
+        oi = np.empty((nq, top_k), np.int64)
+        os_ = np.empty((nq, top_k), np.float32)
+        o64 = np.empty((nq, top_k), np.float64) if with_f64 else None
+        cnt = np.empty(nq, np.int32)
+        self._check(self._lib.rv_index_rank_cascade(self._h, q.ctypes.data, nq, top_k, threshold, oi.ctypes.data,
+                                                    os_.ctypes.data, o64.ctypes.data if with_f64 else None,
+                                                    cnt.ctypes.data))
+        return (oi, os_, cnt, o64) if with_f64 else (oi, os_, cnt)
+
+    def rank_cascade(self, query, top_k: int, threshold: float) -> list[tuple[int, float]]:
+        """``SearchIndex::rank_cascade`` (``index.rs:245-297``): a query of the wrong dimension or
+        an empty index gives no results."""
+        q = np.asarray(query, np.float32).reshape(-1)
+        if q.shape[0] != self.hidden_dim or len(self) == 0 or top_k <= 0:
+            return []
+        oi, os_, cnt = self.topk_cascade(q[None, :], top_k, threshold)
         return [(int(oi[0, i]), float(os_[0, i])) for i in range(int(cnt[0]))]
 
 

@@ -1,10 +1,13 @@
-"""PolarQuant ("TurboQuant") oracle pinned against the reference's own tests of the path, plus the
+"""The two approximate searches of ``SearchIndex`` — PolarQuant ("TurboQuant") and the MRL
+cascade — in the oracle, pinned against the reference's own tests of those paths, plus the
 host-side policy and rotation of the mirror (CPU only).
 
 Reference tests restated: ``rotation_is_orthogonal`` (``turbo_quant.rs:385-398``),
 ``encode_decode_roundtrip`` (``:401-408``), ``corpus_scan_recall_and_throughput`` (``:411-484``),
 ``small_corpus_skips_turboquant_compression`` and ``turboquant_recall_vs_exact``
-(``index.rs:403-410``, ``:555-585``).  The rotations are seeded from numpy's generator, not the
+(``index.rs:403-410``, ``:555-585``), ``cascade_recall_at_10_vs_full_rank``,
+``cascade_falls_back_without_truncated_matrix`` and ``cascade_respects_threshold``
+(``index.rs:487-553``).  The rotations are seeded from numpy's generator, not the
 reference's ChaCha8 stream, so the recall bounds are checked rather than exact values."""
 
 import numpy as np
@@ -120,3 +123,43 @@ def test_rank_turboquant_order_threshold_and_ties():
     assert np.all(np.diff(s64) <= 0)
     idx2, s2 = tq.rank_turboquant(rows, q, 50, 0.2, r)
     assert np.all(s2 >= 0.2) and len(idx2) <= 50
+
+
+# ---------------------------------------------------------------- MRL cascade (index.rs:245-297)
+def test_cascade_recall_at_10_vs_full_rank():
+    """index.rs:487-522: 200 rows of 8 dims, cascade 4, recall@10 >= 0.7."""
+    n, dim = 200, 8
+    emb = sin_vectors(n, dim, 7, 13)
+    q = np.sin((42 * 7 + np.arange(dim) * 13).astype(np.float32)).astype(np.float32)
+    q /= max(np.linalg.norm(q), 1e-12)
+    full = [i for i, _ in scan.rank(emb, q, 0.0)][:10]
+    idx, _ = scan.rank_cascade(emb, q, 10, 0.0, 4)
+    assert len(set(idx.tolist()) & set(full)) >= 7
+
+
+def test_cascade_falls_back_without_truncated_matrix():
+    """index.rs:524-539: without a truncated matrix rank_cascade is rank."""
+    emb = np.array([[0.9, 0.1], [0.1, 0.9]], np.float32)
+    q = np.array([1.0, 0.0], np.float32)
+    idx, s = scan.rank_cascade(emb, q, 10, 0.0, None)
+    plain = scan.rank(emb, q, 0.0)
+    assert idx.tolist() == [i for i, _ in plain]
+    np.testing.assert_allclose(s, [v for _, v in plain], atol=1e-2)  # bf16-rounded rows
+
+
+def test_cascade_respects_threshold():
+    """index.rs:541-553: rows [1, 0] and [0, 1], cascade 1, threshold 0.5 keeps row 0 only."""
+    emb = np.array([[1.0, 0.0], [0.0, 1.0]], np.float32)
+    idx, s = scan.rank_cascade(emb, np.array([1.0, 0.0], np.float32), 10, 0.5, 1)
+    assert idx.tolist() == [0] and s[0] == 1.0
+
+
+def test_cascade_transform_is_layernorm_truncate_normalise():
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((5, 96)).astype(np.float32)
+    y = scan.ln_truncate(x, 32)
+    x64 = x.astype(np.float64)
+    ln = (x64 - x64.mean(1, keepdims=True)) / np.sqrt(x64.var(1, keepdims=True) + 1e-5)
+    ref = ln[:, :32] / np.linalg.norm(ln[:, :32], axis=1, keepdims=True)
+    np.testing.assert_allclose(y, ref, atol=2e-6)
+    np.testing.assert_allclose(np.linalg.norm(y, axis=1), 1.0, atol=1e-6)
