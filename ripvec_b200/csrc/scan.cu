@@ -137,6 +137,8 @@ __global__ void __launch_bounds__(256) rescore_kernel(
     const int64_t r = li[c];
     const __nv_bfloat16* rowp = db + static_cast<size_t>(r - base) * dim;
     double acc = 0.0;
+    // Unrolled so that several 16-byte row loads are in flight ahead of the ordered f64 sum.
+#pragma unroll 8
     for (int d = 0; d < dim; d += 8) {
       const uint4 u = *reinterpret_cast<const uint4*>(rowp + d);
       float f[8];

@@ -117,43 +117,87 @@ __global__ void __launch_bounds__(256) polar_encode_kernel(const __nv_bfloat16* 
 }
 
 // ---------------------------------------------------------------- query tables
-// One CTA per query: rotated query (same order as the rows) and its centroid table
-// lut[q][i][j] = a_i * cos_j + b_i * sin_j (turbo_quant.rs:212-241).
-__global__ void __launch_bounds__(256) polar_lut_kernel(const float* __restrict__ q, int dim,
+// grid (ceil(pairs / 128), nq), 128 threads: thread p of query blockIdx.y rotates its pair of
+// the query (same order as the rows) and writes that pair's centroid table
+// lut[q][p][j] = a_p * cos_j + b_p * sin_j (turbo_quant.rs:212-241).  The d loop is unrolled so
+// that many rotation loads (L2-resident) are in flight ahead of the ordered sums.
+__global__ void __launch_bounds__(128) polar_lut_kernel(const float* __restrict__ q, int dim,
                                                         const float* __restrict__ rt,
                                                         const float* __restrict__ cos_sin, int levels,
                                                         float* __restrict__ lut) {
   extern __shared__ float qs[];
-  const int qi = blockIdx.x;
+  const int qi = blockIdx.y;
   const int pairs = dim / 2;
   for (int d = threadIdx.x; d < dim; d += blockDim.x) qs[d] = q[static_cast<size_t>(qi) * dim + d];
   __syncthreads();
-  for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
-    float a = 0.f, b = 0.f;
-    for (int d = 0; d < dim; ++d) {
-      const float2 r = *reinterpret_cast<const float2*>(rt + static_cast<size_t>(d) * dim + 2 * p);
-      a = __fadd_rn(a, __fmul_rn(qs[d], r.x));
-      b = __fadd_rn(b, __fmul_rn(qs[d], r.y));
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= pairs) return;
+  float a = 0.f, b = 0.f;
+  const float* col = rt + 2 * p;
+  for (int d0 = 0; d0 < dim; d0 += 16) {  // dim is a multiple of 64
+    float2 r[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) r[k] = *reinterpret_cast<const float2*>(col + static_cast<size_t>(d0 + k) * dim);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      a = __fadd_rn(a, __fmul_rn(qs[d0 + k], r[k].x));
+      b = __fadd_rn(b, __fmul_rn(qs[d0 + k], r[k].y));
     }
-    float* out = lut + (static_cast<size_t>(qi) * pairs + p) * levels;
-    for (int j = 0; j < levels; ++j)
-      out[j] = __fadd_rn(__fmul_rn(a, cos_sin[j]), __fmul_rn(b, cos_sin[levels + j]));
   }
+  float* out = lut + (static_cast<size_t>(qi) * pairs + p) * levels;
+  for (int j = 0; j < levels; ++j)
+    out[j] = __fadd_rn(__fmul_rn(a, cos_sin[j]), __fmul_rn(b, cos_sin[levels + j]));
 }
 
 // ---------------------------------------------------------------- scan
-// Warp w of the grid scores row groups g = w, w + warps, ... of [g_begin, g_begin + g_count):
-// lane l owns row 32 g + l.  QB queries per pass share each loaded code word.  Scores go to
-// s[qq * ld + 32 (g - g_begin) + l] for the rows inside the first `valid` of the launch.
+// Threads per scan CTA: the 4-query tables (4 x 24 KB at 768 dims) allow two CTAs per SM, so
+// that variant runs 16 warps per CTA to keep 32 warps of loads in flight per SM.
 template <int QB>
-__global__ void __launch_bounds__(256) polar_scan_kernel(const float4* __restrict__ radii,
-                                                         const uint4* __restrict__ bins, int pairs,
-                                                         int64_t g_begin, int64_t g_count, int64_t valid,
-                                                         const float* __restrict__ lut, int qn,
-                                                         int levels, float* __restrict__ s, int64_t ld) {
-  extern __shared__ float lut_s[];
+constexpr int scan_threads() {
+  return QB == 4 ? 512 : 256;
+}
+
+// QB consecutive table entries (queries q0..q0+QB-1 of one pair and bin) in one shared load.
+template <int QB>
+struct QVec;
+template <>
+struct QVec<1> {
+  __device__ __forceinline__ static void get(const float* p, float (&v)[1]) { v[0] = *p; }
+};
+template <>
+struct QVec<2> {
+  __device__ __forceinline__ static void get(const float* p, float (&v)[2]) {
+    const float2 t = *reinterpret_cast<const float2*>(p);
+    v[0] = t.x;
+    v[1] = t.y;
+  }
+};
+template <>
+struct QVec<4> {
+  __device__ __forceinline__ static void get(const float* p, float (&v)[4]) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    v[0] = t.x;
+    v[1] = t.y;
+    v[2] = t.z;
+    v[3] = t.w;
+  }
+};
+
+// Warp w of the grid scores row groups g = w, w + warps, ... of [g_begin, g_begin + g_count):
+// lane l owns row 32 g + l.  The QB queries of a pass share each loaded code word; their tables
+// sit interleaved in shared memory, lut_s[(pair * levels + bin) * QB + query], so one load
+// brings the entries of all QB queries.  Scores go to s[qq * ld + 32 (g - g_begin) + l] for the
+// rows inside the first `valid` of the launch.
+template <int QB>
+__global__ void __launch_bounds__(scan_threads<QB>()) polar_scan_kernel(
+    const float4* __restrict__ radii, const uint4* __restrict__ bins, int pairs, int64_t g_begin,
+    int64_t g_count, int64_t valid, const float* __restrict__ lut, int levels, float* __restrict__ s,
+    int64_t ld) {
+  extern __shared__ __align__(16) float lut_s[];
   const int tab = pairs * levels;
-  for (int i = threadIdx.x; i < qn * tab; i += blockDim.x) lut_s[i] = lut[i];
+#pragma unroll
+  for (int qq = 0; qq < QB; ++qq)
+    for (int r = threadIdx.x; r < tab; r += blockDim.x) lut_s[r * QB + qq] = lut[qq * tab + r];
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int p4n = pairs / 4, p16n = pairs / 16;
@@ -172,22 +216,22 @@ __global__ void __launch_bounds__(256) polar_scan_kernel(const float4* __restric
 #pragma unroll
       for (int k = 0; k < 4; ++k) rv4[k] = __ldcs(rp + (c * 4 + k) * 32);
       const uint32_t words[4] = {bw.x, bw.y, bw.z, bw.w};
+      const float* row_tab = lut_s + c * 16 * levels * QB;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int code = (words[j >> 2] >> (8 * (j & 3))) & 0xff;
         const float4 r4 = rv4[j >> 2];
         const float rad = (j & 3) == 0 ? r4.x : (j & 3) == 1 ? r4.y : (j & 3) == 2 ? r4.z : r4.w;
-        const int off = (c * 16 + j) * levels + code;
+        float t[QB];
+        QVec<QB>::get(row_tab + (j * levels + code) * QB, t);
 #pragma unroll
-        for (int qq = 0; qq < QB; ++qq)
-          if (QB == 1 || qq < qn) acc[qq] = __fadd_rn(acc[qq], __fmul_rn(rad, lut_s[qq * tab + off]));
+        for (int qq = 0; qq < QB; ++qq) acc[qq] = __fadd_rn(acc[qq], __fmul_rn(rad, t[qq]));
       }
     }
     const int64_t col = g * 32 + lane;
     if (col < valid) {
 #pragma unroll
-      for (int qq = 0; qq < QB; ++qq)
-        if (QB == 1 || qq < qn) s[qq * ld + col] = acc[qq];
+      for (int qq = 0; qq < QB; ++qq) s[qq * ld + col] = acc[qq];
     }
   }
 }
@@ -327,7 +371,7 @@ int scan_qb(int pairs, int levels, int qn) {
 
 template <int QB>
 cudaError_t launch_scan(const float* radii, const uint8_t* bins, int pairs, int64_t g_begin, int64_t g_count,
-                        int64_t valid, const float* lut, int qn, int levels, float* s, int64_t ld, int sms,
+                        int64_t valid, const float* lut, int levels, float* s, int64_t ld, int sms,
                         cudaStream_t st) {
   const size_t smem = size_t(QB) * pairs * levels * sizeof(float);
   static bool attr[64] = {false};
@@ -339,12 +383,18 @@ cudaError_t launch_scan(const float* radii, const uint8_t* bins, int pairs, int6
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  const int64_t blocks_needed = (g_count + 7) / 8;
-  const int64_t cap = int64_t(sms) * 8;
+  constexpr int threads = scan_threads<QB>();
+  constexpr int warps_per_cta = threads / 32;
+  const int64_t blocks_needed = (g_count + warps_per_cta - 1) / warps_per_cta;
+  // One wave of persistent CTAs: as many per SM as the shared tables and threads allow.
+  int per_sm = 0;
+  cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, polar_scan_kernel<QB>, threads, smem);
+  if (oe != cudaSuccess) return oe;
+  const int64_t cap = int64_t(sms) * (per_sm > 0 ? per_sm : 1);
   const int grid = static_cast<int>(blocks_needed < cap ? blocks_needed : cap);
-  polar_scan_kernel<QB><<<grid, 256, smem, st>>>(reinterpret_cast<const float4*>(radii),
-                                                  reinterpret_cast<const uint4*>(bins), pairs, g_begin, g_count,
-                                                  valid, lut, qn, levels, s, ld);
+  polar_scan_kernel<QB><<<grid, threads, smem, st>>>(reinterpret_cast<const float4*>(radii),
+                                                      reinterpret_cast<const uint4*>(bins), pairs, g_begin, g_count,
+                                                      valid, lut, levels, s, ld);
   return cudaGetLastError();
 }
 
@@ -364,6 +414,7 @@ cudaError_t polar_encode(const __nv_bfloat16* x, int64_t n, int dim, const float
 cudaError_t polar_query_tables(const float* q, int nq, int dim, const float* rt, const float* cos_sin, int levels,
                                float* lut, cudaStream_t st) {
   if (nq <= 0) return cudaSuccess;
+  if (nq > 65535) return cudaErrorInvalidValue;
   const size_t smem = size_t(dim) * sizeof(float);
   static bool attr[64] = {false};
   int dev = 0;
@@ -374,7 +425,8 @@ cudaError_t polar_query_tables(const float* q, int nq, int dim, const float* rt,
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  polar_lut_kernel<<<nq, 256, smem, st>>>(q, dim, rt, cos_sin, levels, lut);
+  const dim3 grid(static_cast<unsigned>((dim / 2 + 127) / 128), static_cast<unsigned>(nq));
+  polar_lut_kernel<<<grid, 128, smem, st>>>(q, dim, rt, cos_sin, levels, lut);
   return cudaGetLastError();
 }
 
@@ -387,20 +439,20 @@ cudaError_t polar_scan(const float* radii, const uint8_t* bins, int pairs, int64
   const int64_t g_count = (rows + 31) / 32;
   const size_t tab = size_t(pairs) * levels;
   for (int q0 = 0; q0 < nq; ) {
+    // scan_qb never exceeds the queries left, so every pass scores exactly qb queries.
     const int qb = scan_qb(pairs, levels, nq - q0);
-    const int qn = std::min(qb, nq - q0);
     cudaError_t e;
     if (qb == 4)
-      e = launch_scan<4>(radii, bins, pairs, g_begin, g_count, rows, lut + q0 * tab, qn, levels, s + q0 * ld, ld,
-                         sms, st);
+      e = launch_scan<4>(radii, bins, pairs, g_begin, g_count, rows, lut + q0 * tab, levels, s + q0 * ld, ld, sms,
+                         st);
     else if (qb == 2)
-      e = launch_scan<2>(radii, bins, pairs, g_begin, g_count, rows, lut + q0 * tab, qn, levels, s + q0 * ld, ld,
-                         sms, st);
+      e = launch_scan<2>(radii, bins, pairs, g_begin, g_count, rows, lut + q0 * tab, levels, s + q0 * ld, ld, sms,
+                         st);
     else
-      e = launch_scan<1>(radii, bins, pairs, g_begin, g_count, rows, lut + q0 * tab, qn, levels, s + q0 * ld, ld,
-                         sms, st);
+      e = launch_scan<1>(radii, bins, pairs, g_begin, g_count, rows, lut + q0 * tab, levels, s + q0 * ld, ld, sms,
+                         st);
     if (e != cudaSuccess) return e;
-    q0 += qn;
+    q0 += qb;
   }
   return cudaSuccess;
 }
