@@ -23,8 +23,9 @@ every rank embeds its own 4096 chunks).
 ``--impl reference`` times that CPU port as the reference arm (rank 0 only).  Other workloads:
 ``--workload long`` (config 3, fp16, 512 chunks of 2048..8192 tokens), ``--workload sweep``
 (config 4, 1M log-normal chunks sharded by token count), ``--workload scan`` (config 5, exact
-top-100 over a 10M x 768 bf16 database, 1024 queries, per-shard results merged after one NCCL
-all-gather).
+top-100 over a 10M x 768 bf16 database, 1024 queries by default or a list such as
+``--queries 1,16,64,128``, per-shard results merged after one NCCL all-gather),
+``--workload turboquant`` (``rank_turboquant`` over 4-bit PolarQuant codes of the same database).
 """
 
 from __future__ import annotations

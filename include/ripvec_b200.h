@@ -7,7 +7,10 @@
  *     backend/generic.rs:147-184, and for ClassicBert by backend/cpu.rs:722-748), and
  *   - the exact search (`SearchIndex::new` / `SearchIndex::rank`,
  *     crates/ripvec-core/src/index.rs:76-186, scoring `similarity::rank_all`,
- *     similarity.rs:24-26).
+ *     similarity.rs:24-26), and
+ *   - its two approximate rankings, `SearchIndex::rank_turboquant` over PolarQuant codes
+ *     (index.rs:196-234, turbo_quant.rs) and the MRL cascade `SearchIndex::rank_cascade`
+ *     (index.rs:245-297).
  *
  * Conventions: every entry point returns 0 (RV_OK) on success or a negative RV_E* code; the
  * message of the last failure on a handle is returned by rv_last_error / rv_index_last_error.
