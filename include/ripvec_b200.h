@@ -10,7 +10,7 @@
  *     similarity.rs:24-26), and
  *   - its two approximate rankings, `SearchIndex::rank_turboquant` over PolarQuant codes
  *     (index.rs:196-234, turbo_quant.rs) and the MRL cascade `SearchIndex::rank_cascade`
- *     (index.rs:245-297).
+ *     (index.rs:245-297), and its all-pairs `SearchIndex::find_duplicates` (index.rs:325-348).
  *
  * Conventions: every entry point returns 0 (RV_OK) on success or a negative RV_E* code; the
  * message of the last failure on a handle is returned by rv_last_error / rv_index_last_error.
@@ -217,6 +217,17 @@ int rv_index_cascade_rows(rv_index* idx, float* out);
  * falls back to rank).  top_k in [1, 682].  Outputs as rv_index_topk; host buffers. */
 int rv_index_rank_cascade(rv_index* idx, const float* queries, int32_t nq, int32_t top_k, float threshold,
                           int64_t* out_idx, float* out_score, double* out_score64, int32_t* out_count);
+
+/* ---------------------------------------------------------------- near-duplicate pairs */
+/* SearchIndex::find_duplicates (crates/ripvec-core/src/index.rs:325-348): the pairs (a, b), a < b,
+ * whose exact score (as rv_index_topk: sequential f64 sum of the bf16 products) is >= threshold,
+ * ordered by (score desc, a asc, b asc), at most max_pairs of them.  Fewer than two rows give no
+ * pairs.  Rows are numbered base + local row.  out_a / out_b [max_pairs] int64, out_score
+ * [max_pairs] f32, out_score64 (optional) f64, *out_count = pairs written; host buffers.  At
+ * most 8388608 pairs may score within the f32 error bound of the threshold (about
+ * dim * 2^-22 for unit rows); more returns RV_E_DEVICE (raise the threshold). */
+int rv_index_find_duplicates(rv_index* idx, float threshold, int64_t max_pairs, int64_t* out_a, int64_t* out_b,
+                             float* out_score, double* out_score64, int64_t* out_count);
 
 /* ---------------------------------------------------------------- single-kernel entry points
  * Used by the parity tests to check one kernel against the CPU oracle.  Device pointers. */

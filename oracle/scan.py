@@ -8,7 +8,8 @@ check (wrong or empty query -> no results), scores ``embeddings @ query`` (``sim
 leaves the order of equal scores unspecified; this build fixes it to (score desc, row asc), the
 order ``rrf_fuse`` uses (``hybrid.rs:198-200``).
 
-``ln_truncate`` / ``rank_cascade`` restate the MRL cascade (``index.rs:99-132``, ``:245-297``).
+``ln_truncate`` / ``rank_cascade`` restate the MRL cascade (``index.rs:99-132``, ``:245-297``) and
+``find_duplicates`` the all-pairs search (``index.rs:325-348``).
 
 ``topk_exact`` is the bit-exact definition the GPU scan is checked against: rows and query are
 bf16 values, each score is the sequential sum over d = 0..dim-1 in float64 of the (exact)
@@ -154,6 +155,37 @@ def rank_cascade(rows: np.ndarray, query, top_k: int, threshold: float, cascade_
     cand, exact = cand[keep], exact[keep]
     order = np.lexsort((cand, -exact))[:top_k]
     return cand[order].astype(np.int64), exact[order]
+
+
+def find_duplicates(rows: np.ndarray, threshold: float, max_pairs: int):
+    """``SearchIndex::find_duplicates`` (``index.rs:325-348``): pairs (a, b), a < b, of the
+    bf16-rounded rows whose exact score (sequential f64 sum over d of the bf16 products) is
+    ``>= threshold``, ordered by (score desc, a asc, b asc), at most ``max_pairs``.  Returns
+    ``(a int64 [m], b int64 [m], score f64 [m])``.  The reference scores with one f32 BLAS GEMM
+    and leaves the order of equal scores to ``sort_unstable_by``."""
+    rb = ops.to_bf16(np.asarray(rows, np.float32)).astype(np.float64)
+    n = rb.shape[0]
+    if n < 2 or max_pairs <= 0:
+        e = np.zeros(0, np.int64)
+        return e, e, np.zeros(0, np.float64)
+    thr = np.float64(np.float32(threshold))
+    rt = np.ascontiguousarray(rb.T)
+    aa, bb, ss = [], [], []
+    for r0 in range(0, n - 1, 128):  # upper-triangle row blocks whose accumulators stay in cache
+        r1 = min(n, r0 + 128)
+        acc = np.zeros((r1 - r0, n - r0), np.float64)
+        prod = np.empty_like(acc)
+        for d in range(rb.shape[1]):
+            np.multiply(rt[d, r0:r1, None], rt[d, None, r0:], out=prod)
+            np.add(acc, prod, out=acc)
+        i, j = np.nonzero(acc >= thr)
+        up = (j + r0) > (i + r0)
+        aa.append(i[up] + r0)
+        bb.append(j[up] + r0)
+        ss.append(acc[i[up], j[up]])
+    a, b, sc = np.concatenate(aa), np.concatenate(bb), np.concatenate(ss)
+    order = np.lexsort((b, a, -sc))[:max_pairs]
+    return a[order].astype(np.int64), b[order].astype(np.int64), sc[order]
 
 
 def merge_topk(idx_lists: np.ndarray, score_lists: np.ndarray, k: int, threshold: float = -np.inf):

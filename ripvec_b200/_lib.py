@@ -98,6 +98,7 @@ SIGNATURES = {
     "rv_index_cascade_dim": (C.c_int, [vp]),
     "rv_index_cascade_rows": (C.c_int, [vp, vp]),
     "rv_index_rank_cascade": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
+    "rv_index_find_duplicates": (C.c_int, [vp, f32, i64, vp, vp, vp, vp, vp]),
     "rv_op_gemm": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "rv_op_attention": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, f32, vp]),
     "rv_op_layernorm": (C.c_int, [i32, vp, vp, i32, i32, vp, vp, f32, vp]),

@@ -14,6 +14,7 @@
 #include "../../include/ripvec_b200.h"
 #include "engine.h"
 #include "cascade.h"
+#include "dup.h"
 #include "index_impl.h"
 #include "kernels.h"
 #include "scan.h"
@@ -389,6 +390,9 @@ void rv_index_destroy(rv_index* x) {
     x->c_q.release();
     x->c_os.release();
     x->c_oi.release();
+    x->dup_rec.release();
+    x->dup_cnt.release();
+    x->dup_s64.release();
     if (x->stream) cudaStreamDestroy(x->stream);
   }
   delete x;
@@ -718,6 +722,85 @@ int rv_index_cascade_rows(rv_index* x, float* out) {
     const uint32_t u = uint32_t(h[i]) << 16;
     std::memcpy(out + i, &u, 4);
   }
+  return RV_OK;
+}
+
+int rv_index_find_duplicates(rv_index* x, float threshold, int64_t max_pairs, int64_t* out_a, int64_t* out_b,
+                             float* out_score, double* out_score64, int64_t* out_count) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (!out_count || (max_pairs > 0 && (!out_a || !out_b || !out_score)) || max_pairs < 0)
+    return ifail(x, RV_E_INVALID, "null argument or negative max_pairs");
+  *out_count = 0;
+  if (x->n < 2 || max_pairs == 0) return RV_OK;  // index.rs:327-330
+  Dev g(x->device);
+  cudaStream_t st = x->stream;
+  const int n = static_cast<int>(x->n), dim = x->dim;
+  // Candidate bound: every pair whose exact score reaches the threshold has an f32 tensor-core
+  // score of at least threshold - eps.
+  const double eps = double(dim) * std::ldexp(1.0, -22) * x->max_norm * x->max_norm;
+  const float thr_lo = std::nextafter(static_cast<float>(double(threshold) - eps), -INFINITY);
+  constexpr long long kCap = 1LL << 23;  // candidate records per call (16 bytes each)
+  int strip = 16384;                     // rows per GEMM launch (RV_DUP_STRIP_ROWS for tests)
+  if (const char* e = std::getenv("RV_DUP_STRIP_ROWS")) strip = std::max(128, std::atoi(e) / 128 * 128);
+  if (!x->dup_rec.reserve(size_t(kCap)) || !x->dup_cnt.reserve(1))
+    return ifail(x, RV_E_NOMEM, "duplicate candidate buffer allocation failed");
+  IX_TRY(x, cudaMemsetAsync(x->dup_cnt.p, 0, sizeof(unsigned long long), st));
+  for (int r0 = 0; r0 < n; r0 += strip) {
+    const int rows = std::min(strip, n - r0);
+    const int cols = (n - r0 + 255) / 256 * 256;
+    CUtensorMap ts;
+    std::string why;
+    if (!rv::make_tmap_2d_16bit(&ts, x->db + size_t(r0) * dim, true, dim, uint64_t(rows), uint64_t(dim) * 2, 64,
+                                128, &why))
+      return ifail(x, RV_E_CUDA, why);
+    IX_TRY(x, rv::dup_candidates(ts, x->tmap_db, rows, cols, dim, r0, n, thr_lo, x->dup_rec.p, x->dup_cnt.p, kCap,
+                                 x->d_err, st));
+    x->launches++;
+  }
+  unsigned long long m = 0;
+  unsigned int e = 0;
+  IX_TRY(x, cudaMemcpyAsync(&m, x->dup_cnt.p, sizeof(m), cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaMemcpyAsync(&e, x->d_err, 4, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaStreamSynchronize(st));
+  if (e) {
+    cudaMemset(x->d_err, 0, 4);
+    return ifail(x, RV_E_DEVICE, "duplicate search kernel reported device error flags " + std::to_string(e));
+  }
+  if (m > static_cast<unsigned long long>(kCap))
+    return ifail(x, RV_E_DEVICE,
+                 std::to_string(m) + " pairs score within the error bound of the threshold (more than " +
+                     std::to_string(kCap) + "); raise the threshold");
+  std::vector<int4> rec(m);
+  std::vector<double> s64(m);
+  if (m > 0) {
+    if (!x->dup_s64.reserve(size_t(m))) return ifail(x, RV_E_NOMEM, "duplicate score buffer allocation failed");
+    IX_TRY(x, rv::dup_rescore(x->db, dim, x->dup_rec.p, static_cast<long long>(m), x->dup_s64.p, st));
+    x->launches++;
+    IX_TRY(x, cudaMemcpyAsync(rec.data(), x->dup_rec.p, sizeof(int4) * m, cudaMemcpyDeviceToHost, st));
+    IX_TRY(x, cudaMemcpyAsync(s64.data(), x->dup_s64.p, sizeof(double) * m, cudaMemcpyDeviceToHost, st));
+    IX_TRY(x, cudaStreamSynchronize(st));
+  }
+  // Keep exact scores >= threshold; order (score desc, a asc, b asc); the best max_pairs.
+  std::vector<size_t> keep;
+  keep.reserve(m);
+  for (size_t t = 0; t < m; ++t)
+    if (s64[t] >= double(threshold)) keep.push_back(t);
+  auto before = [&](size_t u, size_t v) {
+    if (s64[u] != s64[v]) return s64[u] > s64[v];
+    if (rec[u].x != rec[v].x) return rec[u].x < rec[v].x;
+    return rec[u].y < rec[v].y;
+  };
+  const size_t out_n = std::min<size_t>(keep.size(), size_t(max_pairs));
+  std::partial_sort(keep.begin(), keep.begin() + out_n, keep.end(), before);
+  for (size_t t = 0; t < out_n; ++t) {
+    const size_t u = keep[t];
+    out_a[t] = x->base + rec[u].x;
+    out_b[t] = x->base + rec[u].y;
+    out_score[t] = static_cast<float>(s64[u]);
+    if (out_score64) out_score64[t] = s64[u];
+  }
+  *out_count = static_cast<int64_t>(out_n);
   return RV_OK;
 }
 

@@ -65,6 +65,10 @@ struct rv_index {
   rv_index* cascade = nullptr;
   DevBuf<float> c_q, c_os;
   DevBuf<int64_t> c_oi;
+  // find_duplicates (dup.cu): candidate pair records, their counter and exact scores.
+  DevBuf<int4> dup_rec;
+  DevBuf<unsigned long long> dup_cnt;
+  DevBuf<double> dup_s64;
   int64_t launches = 0;
   bool filter_off = false;  // RV_SCAN_FILTER=0 at creation
 };

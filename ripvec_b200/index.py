@@ -233,6 +233,27 @@ class SearchIndex:
         return [(int(oi[0, i]), float(os_[0, i])) for i in range(int(cnt[0]))]
 
 
+    # ------------------------------------------------------------ near-duplicate pairs
+    def duplicate_pairs(self, threshold: float, max_pairs: int):
+        """``find_duplicates`` as arrays: ``(a int64 [m], b int64 [m], score f32 [m], score f64 [m])``."""
+        mp = max(int(max_pairs), 0)
+        a = np.empty(max(mp, 1), np.int64)
+        b = np.empty(max(mp, 1), np.int64)
+        s = np.empty(max(mp, 1), np.float32)
+        s64 = np.empty(max(mp, 1), np.float64)
+        cnt = C.c_int64(0)
+        self._check(self._lib.rv_index_find_duplicates(self._h, threshold, mp, a.ctypes.data, b.ctypes.data,
+                                                       s.ctypes.data, s64.ctypes.data, C.byref(cnt)))
+        m = int(cnt.value)
+        return a[:m], b[:m], s[:m], s64[:m]
+
+    def find_duplicates(self, threshold: float, max_pairs: int) -> list[tuple[int, int, float]]:
+        """``SearchIndex::find_duplicates`` (``index.rs:325-348``): ``(a, b, similarity)`` with
+        a < b and similarity >= threshold, sorted by descending similarity, at most ``max_pairs``."""
+        a, b, s, _ = self.duplicate_pairs(threshold, max_pairs)
+        return [(int(x), int(y), float(z)) for x, y, z in zip(a, b, s)]
+
+
 def merge_topk_device(idx_lists, score64_lists, k: int, threshold: float = float("-inf"), device: int = 0,
                       stream: int = 0):
     """Merges per-shard device results ``[n_lists, nq, k]`` (int64 idx, f64 scores) on the GPU;

@@ -163,3 +163,31 @@ def test_cascade_transform_is_layernorm_truncate_normalise():
     ref = ln[:, :32] / np.linalg.norm(ln[:, :32], axis=1, keepdims=True)
     np.testing.assert_allclose(y, ref, atol=2e-6)
     np.testing.assert_allclose(np.linalg.norm(y, axis=1), 1.0, atol=1e-6)
+
+
+# ---------------------------------------------------------------- find_duplicates (index.rs:325-348)
+def test_find_duplicates_contract():
+    """Fewer than two rows give nothing; pairs have a < b, scores >= threshold, sorted by
+    descending score then (a, b); max_pairs truncates."""
+    assert scan.find_duplicates(np.zeros((1, 4), np.float32), 0.0, 10)[0].size == 0
+    e = np.array([[1, 0, 0], [1, 0, 0], [0, 1, 0], [0.6, 0.8, 0]], np.float32)
+    a, b, s = scan.find_duplicates(e, 0.5, 10)
+    assert list(zip(a.tolist(), b.tolist())) == [(0, 1), (2, 3), (0, 3), (1, 3)]
+    np.testing.assert_allclose(s, [1.0, 0.80078125, 0.6015625, 0.6015625])  # bf16 0.6 / 0.8
+    a2, b2, _ = scan.find_duplicates(e, 0.5, 2)
+    assert list(zip(a2.tolist(), b2.tolist())) == [(0, 1), (2, 3)]
+    assert scan.find_duplicates(e, 1.5, 10)[0].size == 0
+
+
+def test_find_duplicates_matches_a_float64_gram_matrix():
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((200, 32)).astype(np.float32)
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    x[150] = x[3]
+    a, b, s = scan.find_duplicates(x, 0.3, 10**6)
+    from oracle import ops
+    g = ops.to_bf16(x).astype(np.float64) @ ops.to_bf16(x).astype(np.float64).T
+    iu = np.triu_indices(200, k=1)
+    assert len(a) == int((g[iu] >= np.float32(0.3)).sum())
+    np.testing.assert_allclose(s, g[a, b], rtol=1e-12)
+    assert (a[0], b[0]) == (3, 150) and np.all(np.diff(s) <= 0) and np.all(a < b)
