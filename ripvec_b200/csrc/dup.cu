@@ -3,7 +3,8 @@
 // BLAS GEMM and keeps the upper-triangle pairs scoring at least the threshold.
 //
 // Here the same products come from the tcgen05 GEMM in strips of rows (A = rows [r0, r0 + R),
-// B = rows [r0, n), so only the upper triangle and its diagonal blocks are computed), and the
+// B = rows [r0, n), so only the upper triangle and its diagonal blocks are computed; tiles are
+// walked column block by column block, so the strip stays in L2 and B streams once), and the
 // epilogue keeps a pair (i, j > i) whose f32 score is at least threshold - eps, eps a bound on
 // the f32 accumulation error (dim * 2^-22 * max row norm^2).  No matrix leaves the SM: a kept
 // pair is a {i, j, f32 score} record at a slot from one global counter per warp.  Each record is
@@ -48,6 +49,9 @@ struct EpiPairFilter {
   int n;
   using Pre = NoPre;
   using Tile = NoTile;
+  // B (the rows from r0 on, up to n x 1536 bytes) outgrows L2 while A (one strip) fits: walk the
+  // tiles column block by column block so that each B tile comes from HBM once.
+  static constexpr bool kColumnMajorTiles = true;
   __device__ __forceinline__ void stage(float*, int, int) const {}
   __device__ __forceinline__ void tile_load(Tile&, int, int) const {}
   __device__ __forceinline__ void load(Pre&, int, int) const {}

@@ -54,6 +54,27 @@ struct HasFinish : std::false_type {};
 template <class E>
 struct HasFinish<E, std::void_t<decltype(std::declval<const E&>().finish(0))>> : std::true_type {};
 
+// Optional epilogue constant `kColumnMajorTiles = true`: persistent CTAs walk the tiles column
+// block by column block (all row blocks of one B tile, then the next) instead of row block by row
+// block.  For a GEMM whose B operand is larger than L2 and whose A operand fits in it, each B
+// tile is then read from HBM once instead of once per row block.
+template <class E, class = void>
+struct ColumnMajorTiles : std::false_type {};
+template <class E>
+struct ColumnMajorTiles<E, std::void_t<decltype(E::kColumnMajorTiles)>>
+    : std::integral_constant<bool, E::kColumnMajorTiles> {};
+
+template <class Epi>
+__device__ __forceinline__ void tile_origin(int t, int num_m, int num_n, int bn, int& m0, int& n0) {
+  if constexpr (ColumnMajorTiles<Epi>::value) {
+    m0 = (t % num_m) * kGemmBM;
+    n0 = (t / num_m) * bn;
+  } else {
+    m0 = (t / num_n) * kGemmBM;
+    n0 = (t % num_n) * bn;
+  }
+}
+
 template <typename T>
 struct EpiStore {
   T* c;
@@ -321,8 +342,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t issued = 0, issued_parity = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int m0 = (t / num_n) * kGemmBM;
-        const int n0 = (t % num_n) * BN;
+        int m0, n0;
+        tile_origin<Epi>(t, num_m, num_n, BN, m0, n0);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
@@ -391,8 +412,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      const int m0 = (t / num_n) * kGemmBM;
-      const int n0 = (t % num_n) * BN;
+      int m0, n0;
+      tile_origin<Epi>(t, num_m, num_n, BN, m0, n0);
       const int row = m0 + quad * 32 + lane;
       const bool live = row < M;
       typename Epi::Pre pre[2];
