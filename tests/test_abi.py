@@ -47,6 +47,27 @@ def test_null_arguments_are_rejected_without_a_device(lib):
     assert lib.rv_last_error(None) == b"null context"
 
 
+def test_search_entry_points_reject_a_null_index_without_a_device(lib):
+    """Every PolarQuant, cascade and duplicate-pair entry point checks its handle before touching
+    a device."""
+    import ctypes as C
+
+    inv = _lib.RV_E_INVALID
+    assert lib.rv_index_build_polar(None, None, 4) == inv
+    assert lib.rv_index_has_polar(None) == 0
+    assert lib.rv_index_polar_export(None, None, None) == inv
+    assert lib.rv_index_polar_scores(None, None, 1, None) == inv
+    assert lib.rv_index_rank_turboquant(None, None, 1, 10, 0.0, None, None, None, None) == inv
+    assert lib.rv_index_rank_turboquant_device(None, None, 1, 10, 0.0, None, None, None, None) == inv
+    assert lib.rv_index_build_cascade(None, 64) == inv
+    assert lib.rv_index_cascade_dim(None) == 0
+    assert lib.rv_index_cascade_rows(None, None) == inv
+    assert lib.rv_index_rank_cascade(None, None, 1, 10, 0.0, None, None, None, None) == inv
+    cnt = C.c_int64(-1)
+    assert lib.rv_index_find_duplicates(None, 0.85, 20, None, None, None, None, C.byref(cnt)) == inv
+    assert lib.rv_index_last_error(None) == b"null index"
+
+
 def test_model_desc_layout_matches_header(tmp_path):
     """The ctypes mirror of rv_model_desc has the size and field offsets a C compiler gives."""
     import ctypes as C
