@@ -27,7 +27,8 @@ top-100 over a 10M x 768 bf16 database, 1024 queries by default or a list such a
 ``--queries 1,16,64,128``, per-shard results merged after one NCCL all-gather),
 ``--workload turboquant`` (``rank_turboquant`` over 4-bit PolarQuant codes of the same database),
 ``--workload duplicates`` (``find_duplicates`` over 200k x 768 rows: every pair scored),
-``--workload cascade`` (``rank_cascade`` over the 10M x 768 database truncated to 256 dimensions).
+``--workload cascade`` (``rank_cascade`` over the 10M x 768 database truncated to 256 dimensions),
+``--workload classic`` (config 1: BERT-small over 64 chunks, with its cosine against the fp32 oracle).
 """
 
 from __future__ import annotations
@@ -58,7 +59,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["encoder", "long", "sweep", "scan", "turboquant", "duplicates",
-                                           "cascade"], default="encoder")
+                                           "cascade", "classic"], default="encoder")
     ap.add_argument("--chunks", type=int, default=None, help="override chunks per GPU")
     ap.add_argument("--max-batch-tokens", type=int, default=1 << 19)
     ap.add_argument("--scan-rows", type=int, default=10_000_000,
@@ -671,6 +672,94 @@ def run_duplicates(args):
     idx.close()
 
 
+def classic_workload():
+    """BERT-small (12 layers, hidden 384, 12 heads, FFN 1536, learned positions,
+    post-LN), random-init N(0, 0.02) weights, 64 chunks of U[32, 256] tokens, mean pooling."""
+    from ripvec_b200 import BERT_SMALL, synth
+
+    lengths = synth.uniform_lengths(64, 32, 256, seed=1100)
+    ids, cu = synth.packed_ids(lengths, BERT_SMALL.vocab, seed=1200)
+    return BERT_SMALL, synth.random_weights(BERT_SMALL, seed=1), lengths, ids, cu
+
+
+def classic_oracle(spec, w, ids, cu):
+    """The numpy port of the reference's fp32 ClassicBert CPU path over every chunk, timed."""
+    from oracle import classic_bert
+
+    cfg = classic_bert.ClassicBertConfig(hidden=spec.hidden, num_layers=spec.num_layers, num_heads=spec.num_heads,
+                                         intermediate=spec.intermediate, vocab=spec.vocab,
+                                         max_position=spec.max_position, type_vocab=spec.type_vocab,
+                                         norm_eps=spec.norm_eps)
+    t0 = time.perf_counter()
+    ref = classic_bert.embed_batch(w, cfg, ids, cu, "mean")
+    return ref, time.perf_counter() - t0
+
+
+def run_classic(args):
+    """BASELINE config 1 on the GPU (f16 storage, f32 accumulation) next to the reference's fp32
+    CPU path: tokens/s device-resident and through rv_embed_varlen, and the per-chunk cosine of
+    the GPU embeddings against the fp32 oracle (bar 0.9999 for this fp32 configuration)."""
+    import torch
+
+    from ripvec_b200 import EmbedBackend
+
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    spec, w, lengths, ids, cu = classic_workload()
+    tokens, n = int(cu[-1]), len(lengths)
+    be = EmbedBackend(spec, w, dtype="f16", device=local, pooling="mean")
+    stream = torch.cuda.current_stream()
+    ids_dev = torch.from_numpy(ids).cuda()
+    out_dev = torch.empty(n, spec.hidden, device="cuda", dtype=torch.float32)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
+    for _ in range(args.warmup):
+        be.embed_device(ids_dev, cu, out_dev, stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(physical_gpu(local))
+    sampler.start()
+    launches0 = be.kernel_launches()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for st in range(args.steps):
+        flush.zero_()
+        evs[st][0].record(stream)
+        be.embed_device(ids_dev, cu, out_dev, stream=stream.cuda_stream)
+        evs[st][1].record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    launches = be.kernel_launches() - launches0
+    ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    out_h = np.empty((n, spec.hidden), np.float32)
+    cu_h = np.ascontiguousarray(cu, np.int32)
+    be.embed_packed(ids, cu_h, out_h)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        be.embed_packed(ids, cu_h, out_h)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    be.close()
+    ref, cpu_s = classic_oracle(spec, w, ids, cu)
+    a = out_h.astype(np.float64)
+    b = ref.astype(np.float64)
+    cos = (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+    line = {"metric": "embedded tokens/sec (BERT-small ClassicBert, 64 chunks)", "value": tokens / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded random token ids, random-init N(0,0.02) weights)",
+            "config": {"workload": "classicbert_small_config1", "model": "BERT-small (12L, H384, 12x32, FFN 1536)",
+                       "chunks": n, "lengths": "U[32,256]", "tokens": tokens, "pooling": "mean",
+                       "l2": "flushed between steps (256 MiB write)"},
+            "e2e": {"value": tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(tokens * 4 + 4 * (n + 1)),
+                    "d2h_bytes_per_step": int(n * spec.hidden * 4),
+                    "how": "rv_embed_varlen with host ids / cu_seqlens / output, host clock around the call"},
+            "gpu_launches": int(launches), "clocks": clocks,
+            "parity": {"min_cos": float(cos.min()), "p50_cos": float(np.median(cos)), "bar": 0.9999,
+                       "against": "numpy fp32 port of the reference CPU path, all 64 chunks"},
+            "cpu_baseline": {"value": tokens / cpu_s, "unit": "tokens/s", "cores": blas_threads(), "kind": "port",
+                             "sample": f"all {n} chunks ({tokens} tokens, {cpu_s:.1f} s), numpy fp32 port"}}
+    print(json.dumps(line), flush=True)
+
+
 def run_cascade(args):
     """rank_cascade over a 10M x 768 database truncated to 256 dimensions (1 GPU): one step = one
     call for the query batch, top_k 10 (first phase: the exact top 100 of the truncated rows;
@@ -741,6 +830,8 @@ def main():
         return run_duplicates(args)
     if args.workload == "cascade":
         return run_cascade(args)
+    if args.workload == "classic":
+        return run_classic(args)
     return run_encoder(args)
 
 
