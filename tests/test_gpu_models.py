@@ -150,6 +150,19 @@ def test_bert_small_matches_oracle(cuda_device):
     be.close()
 
 
+def test_bert_small_f16_meets_the_fp32_bar(cuda_device):
+    """BASELINE config 1 is an fp32 configuration: with f16 storage (f32 accumulation) every
+    chunk's embedding has cosine >= 0.9999 against the fp32 oracle."""
+    w = synth.random_weights(BERT_SMALL, seed=9)
+    lengths = synth.uniform_lengths(6, 32, 256, seed=12)
+    ids, cu = synth.packed_ids(lengths, BERT_SMALL.vocab, seed=13)
+    be = EmbedBackend(BERT_SMALL, w, dtype="f16", pooling="mean")
+    out = be.embed_packed(ids, cu)
+    ref = classic_bert.embed_batch(w, classic_cfg(BERT_SMALL), ids, cu, "mean")
+    assert row_cosines(out, ref).min() >= 0.9999
+    be.close()
+
+
 def _write_safetensors(path: Path, tensors: dict, dtype: str = "F32"):
     header, blobs, off = {}, [], 0
     for name, arr in tensors.items():
