@@ -44,7 +44,38 @@ def main():
     db, q = scan_small_inputs()
     idx, s64, cnt = scan.topk_exact(db, q, 10)
     np.savez_compressed(OUT / "scan_small.npz", idx=idx, s64=s64, k=10)
+
+    np.savez_compressed(OUT / "approx_search_small.npz", **approx_search_fixture())
     print("written to", OUT)
+
+
+def approx_search_inputs():
+    """600 x 128 normalised Gaussian rows (row 400 = row 9) and three queries (the last = row 9)."""
+    db = synth.normalized_gaussian(600, 128, seed=61)
+    db[400] = db[9]
+    q = synth.normalized_gaussian(3, 128, seed=62)
+    q[2] = db[9]
+    return db, q
+
+
+def approx_search_fixture() -> dict:
+    """PolarQuant codes (bins, and radii as a checksum of their bits), approximate scores and
+    rank_turboquant results; rank_cascade results; find_duplicates pairs."""
+    from oracle import turbo_quant as tq
+
+    db, q = approx_search_inputs()
+    rot = tq.generate_rotation(128, 42)
+    radii, bins = tq.encode(db, rot)
+    out = {"bins": bins, "radii_bits_sum": np.uint64(radii.view(np.uint32).astype(np.uint64).sum()),
+           "approx": np.stack([tq.scan_corpus(radii, bins, tq.prepare_query(x, rot)) for x in q])}
+    for name, fn in (("tq", lambda x: tq.rank_turboquant(db, x, 5, -np.inf, rot, codes=(radii, bins))),
+                     ("cascade", lambda x: scan.rank_cascade(db, x, 5, -np.inf, 64))):
+        res = [fn(x) for x in q]
+        out[f"{name}_idx"] = np.stack([r[0] for r in res])
+        out[f"{name}_s64"] = np.stack([r[1] for r in res])
+    a, b, s = scan.find_duplicates(db, 0.3, 50)
+    out.update(dup_a=a, dup_b=b, dup_s64=s)
+    return out
 
 
 if __name__ == "__main__":

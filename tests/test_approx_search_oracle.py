@@ -191,3 +191,22 @@ def test_find_duplicates_matches_a_float64_gram_matrix():
     assert len(a) == int((g[iu] >= np.float32(0.3)).sum())
     np.testing.assert_allclose(s, g[a, b], rtol=1e-12)
     assert (a[0], b[0]) == (3, 150) and np.all(np.diff(s) <= 0) and np.all(a < b)
+
+
+def test_golden_approx_search_fixture_reproduces():
+    """The committed fixture (tests/golden/make_golden.py) still matches the oracle bit for bit:
+    PolarQuant bins and radii, approximate scores, rank_turboquant, rank_cascade, find_duplicates."""
+    import sys
+    from pathlib import Path
+
+    golden = Path(__file__).resolve().parent / "golden"
+    sys.path.insert(0, str(golden))
+    from make_golden import approx_search_fixture
+
+    g = np.load(golden / "approx_search_small.npz")
+    now = approx_search_fixture()
+    assert set(g.files) == set(now)
+    for k in g.files:
+        np.testing.assert_array_equal(np.asarray(now[k]), g[k], err_msg=k)
+    assert g["tq_idx"][2, 0] == 9 and g["tq_idx"][2, 1] == 400  # the duplicated row, lowest first
+    assert (g["dup_a"][0], g["dup_b"][0]) == (9, 400)
