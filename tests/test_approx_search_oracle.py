@@ -12,7 +12,7 @@ reference's ChaCha8 stream, so the recall bounds are checked rather than exact v
 
 import numpy as np
 
-from oracle import scan
+from oracle import ops, scan
 from oracle import turbo_quant as tq
 from ripvec_b200.index import polar_rotation, turboquant_eligible
 
@@ -210,3 +210,25 @@ def test_golden_approx_search_fixture_reproduces():
         np.testing.assert_array_equal(np.asarray(now[k]), g[k], err_msg=k)
     assert g["tq_idx"][2, 0] == 9 and g["tq_idx"][2, 1] == 400  # the duplicated row, lowest first
     assert (g["dup_a"][0], g["dup_b"][0]) == (9, 400)
+
+
+def test_polar_scan_is_the_dot_product_with_decoded_rows():
+    """scan_corpus(prepare_query(q)) = (R q) . decode(codes), where a pair (r, bin j) decodes to
+    r (cos theta_j, sin theta_j) (turbo_quant.rs:212-241, :248-289): checked in f64."""
+    dim = 64
+    rng = np.random.default_rng(8)
+    rows = rng.standard_normal((50, dim)).astype(np.float32)
+    rows /= np.linalg.norm(rows, axis=1, keepdims=True)
+    q = rng.standard_normal(dim).astype(np.float32)
+    r = tq.generate_rotation(dim, 3)
+    radii, bins = tq.encode(rows, r)
+    approx = tq.scan_corpus(radii, bins, tq.prepare_query(q, r))
+    theta = bins.astype(np.float64) / 16 * 2 * np.pi - np.pi
+    dec = np.empty((50, dim))
+    dec[:, 0::2] = radii * np.cos(theta)
+    dec[:, 1::2] = radii * np.sin(theta)
+    expect = dec @ (r.astype(np.float64) @ q.astype(np.float64))
+    np.testing.assert_allclose(approx, expect, atol=2e-5)
+    # and the decoded rows approximate the rotated rows (4-bit angles: error below 2 pi / 16)
+    rot = ops.to_bf16(rows).astype(np.float64) @ r.astype(np.float64).T
+    assert np.abs(dec - rot).max() < np.abs(rot).max() * 2 * np.pi / 16 + 1e-6
