@@ -1,6 +1,7 @@
 """Host-side logic of the N > 1 paths, run as world_size-2 gloo process groups on the CPU:
-token-count sharding of the encoder chunks and the search protocol (row-range shards with
-global row numbers, one all-gather of per-shard top-k lists, merge by (score desc, row asc))."""
+token-count sharding of the encoder chunks, the search protocol (row-range shards with global row
+numbers, one all-gather of per-shard top-k lists, merge by (score desc, row asc)), and a rank that
+leaves before the exchange (an error on the survivor within the process-group timeout)."""
 
 import os
 import socket
@@ -73,6 +74,56 @@ def test_two_rank_search_merge_and_encoder_sharding():
         assert ok, f"rank {rank}: merged top-k differs from the global top-k"
         assert total == 5000
         assert abs(tokens[0] - tokens[1]) <= 1024  # greedy balance is within one chunk
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 leaves before the search exchange (as a rank that raised would); rank 0 must get an
+    error from its all-gather within the process-group timeout, not wait forever."""
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()  # flush the message before the abrupt exit
+        os._exit(0)  # no destroy_process_group: the rank is simply gone
+    t0 = time.perf_counter()
+    li = np.zeros((2, 5), np.int64)
+
+    def all_gather(a):
+        t = torch.from_numpy(np.ascontiguousarray(a))
+        out = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [o.numpy() for o in out]
+
+    try:
+        shard.gather_and_merge(li, li.astype(np.float64), 5, scan.merge_topk, all_gather)
+        q.put((rank, "no error"))
+    except Exception as e:  # gloo reports the missing peer or the timeout
+        q.put((rank, f"error after {time.perf_counter() - t0:.1f} s: {type(e).__name__}"))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+@pytest.mark.timeout(120)
+def test_missing_rank_surfaces_as_an_error_not_a_hang():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=90) for _ in range(world))
+    for p in procs:
+        p.join(timeout=30)
+    assert res[1] == "left"
+    assert res[0].startswith("error after"), res[0]
+    assert float(res[0].split()[2]) < 60
 
 
 def test_shard_by_tokens_partitions_and_balances():
