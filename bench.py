@@ -69,6 +69,7 @@ def parse_args():
                          "each, same database); the roofline is HBM below ~210 queries, tensor above")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the 16-chunk oracle check of the timed output")
     return ap.parse_args()
 
 
@@ -184,6 +185,28 @@ def sweep_shard(rank, world, n_chunks):
 
 
 # ------------------------------------------------------------------ reference arm (CPU port)
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def pin_blas_threads() -> int:
+    """Gives the BLAS pool every host core this process may run on and returns the count.
+
+    torchrun exports OMP_NUM_THREADS=1, which OpenBLAS reads when it loads, so without this the
+    reference arm of a multi-rank launch would run on one core."""
+    n = host_cores()
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=n, user_api="blas")
+    except Exception:
+        pass
+    return blas_threads()
+
+
 def blas_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -217,6 +240,18 @@ def cpu_encoder_rate(spec, w, lengths, ids, cu, budget_s: float, dtype=np.float3
     return tok / dt, n, tok, dt
 
 
+def cpu_embed_one(spec, w, ids_one):
+    """One chunk's embedding from the numpy fp32 port of the reference CPU path (f64 result)."""
+    from oracle import modern_bert
+
+    cfg = modern_bert.ModernBertConfig(
+        hidden=spec.hidden, num_layers=spec.num_layers, num_heads=spec.num_heads, intermediate=spec.intermediate,
+        vocab=spec.vocab, max_position=spec.max_position, global_every_n=spec.global_every_n,
+        local_window=spec.local_window, global_rope_theta=spec.global_rope_theta,
+        local_rope_theta=spec.local_rope_theta, norm_eps=spec.norm_eps)
+    return modern_bert.embed_sequence(w, cfg, ids_one).astype(np.float64)
+
+
 def run_reference(args):
     rank, world, local = dist_env()
     if rank != 0:
@@ -227,7 +262,7 @@ def run_reference(args):
 
     spec, name, dtype, desc, lengths, ids, cu = encoder_workload(args, 0)
     w = synth.random_weights(spec, seed=1)
-    cores = blas_threads()
+    cores = pin_blas_threads()
     step_budget = 4.0
     rates, samples = [], []
     for s in range(args.warmup + args.steps):
@@ -257,7 +292,7 @@ def run_reference_scan(args):
     from ripvec_b200 import synth
 
     n_rows, dim, nq = 10_000_000, 768, 1024
-    cores = blas_threads()
+    cores = pin_blas_threads()
     # bounded sample: the reference algorithm (f32 GEMV + full sort) over a slice of the database
     sample = 200_000
     db = synth.normalized_gaussian(sample, dim, seed=77)
@@ -416,10 +451,33 @@ def run_encoder(args):
             raise RuntimeError("e2e outputs are not unit-norm")
 
     cpu = None
+    parity = None
+    if rank == 0 and not args.no_parity:
+        # Parity of the timed workload itself: the device-resident path's output of the last timed
+        # step against the numpy fp32 port of the reference CPU path, on 16 chunks (4 of the long
+        # workload) spread evenly over the rank's chunks, after the timed region.
+        w = synth.random_weights(spec, seed=1)
+        pin_blas_threads()
+        out_last = out_dev.cpu().numpy()
+        n_pick = 4 if args.workload == "long" else 16  # long chunks cost ~10 s each in the oracle
+        pick = np.unique(np.linspace(0, n - 1, min(n_pick, n)).astype(np.int64))
+        cos = []
+        for b in pick:
+            ref = cpu_embed_one(spec, w, ids[cu[b]:cu[b + 1]])
+            g = out_last[b].astype(np.float64)
+            cos.append(float(g @ ref / max(np.linalg.norm(g) * np.linalg.norm(ref), 1e-300)))
+        bar = 0.999 if dtype == "bf16" else 0.9999
+        parity = {"min_cos": min(cos), "p50_cos": float(np.median(cos)), "bar": bar, "chunks": len(pick),
+                  "sample_lengths": [int(lengths[b]) for b in pick],
+                  "against": "numpy fp32 port of the reference CPU path (oracle/modern_bert.py), device-resident "
+                             "output of the last timed step"}
+        if min(cos) < bar:
+            raise RuntimeError(f"parity below the bar on the timed workload: {parity}")
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("encoder", "long"):
         w = synth.random_weights(spec, seed=1)
+        cores = pin_blas_threads()
         r, nc, tok, dt = cpu_encoder_rate(spec, w, lengths, ids, cu, 12.0)
-        cpu = {"value": r, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+        cpu = {"value": r, "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"first {nc} chunks of the workload ({tok} tokens, {dt:.1f} s), numpy fp32 port of the reference CPU path"}
 
     if dist is not None:
@@ -434,7 +492,7 @@ def run_encoder(args):
                            "global_batch": n * world, "seq_len": "varlen", "parallelism": f"dp{world}",
                            "max_batch_tokens": args.max_batch_tokens, "l2": "flushed between steps (256 MiB write)"},
                 "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "cpu_baseline": cpu,
-                "clocks": clocks, "kernels": kernels,
+                "parity": parity, "clocks": clocks, "kernels": kernels,
                 "whole_step_tflops": whole_flops / (total_ms / args.steps / 1e3) / 1e12,
                 "attention_tflops": (att["flops"] / (att["ms"] / 1e3) / 1e12) if att["ms"] else None}
         print(json.dumps(line), flush=True)

@@ -144,6 +144,15 @@ int rv_index_topk(rv_index* idx, const float* queries, int32_t nq, int32_t k, fl
 int rv_index_topk_device(rv_index* idx, const float* queries_dev, int32_t nq, int32_t k,
                          float threshold, int64_t* out_idx_dev, float* out_score_dev,
                          double* out_score64_dev, void* stream);
+/* SearchIndex::rank in full (crates/ripvec-core/src/index.rs:172-186): every row whose exact
+ * score (as rv_index_topk) is >= threshold, ordered by (score desc, row asc); no cap on the
+ * number of rows (MCP find_similar ranks at threshold 0.0 and pages through the whole result,
+ * ripvec-mcp/src/tools.rs:563-570).  query: host f32 [dim].  The first min(count, capacity)
+ * results go to out_idx / out_score (/ out_score64 when non-null), host buffers; *out_count
+ * receives the total count, so a caller can size its buffers with capacity = 0 (or rv_index_size)
+ * first.  threshold = -inf ranks every row. */
+int rv_index_rank(rv_index* idx, const float* query, float threshold, int64_t capacity, int64_t* out_idx,
+                  float* out_score, double* out_score64, int64_t* out_count);
 /* Merges n_lists per-shard results [n_lists, nq, k] (device; idx int64, score f64, as returned
  * by rv_index_topk_device) into the global top k per query, ordered by (score desc, idx asc). */
 int rv_topk_merge_device(int device, const int64_t* idx_in, const double* score_in,
@@ -154,7 +163,7 @@ int rv_topk_merge_device(int device, const int64_t* idx_in, const double* score_
  * (a host whose allocator or memory pool owns the whole device budget, or a serving thread that
  * must not let cudaMalloc / cudaFree synchronise the device).  No counterpart in the reference:
  * it exists only for such callers.  All scratch lives in one fixed device array inside the
- * library (about 4.2 MiB, held by every GPU that loads the library until exit); the call makes
+ * library (about 5 MiB, held by every GPU that loads the library until exit); the call makes
  * no cudaMalloc / cudaFree.  Limits: nq <= 16 queries, k <= 64, rows of at most 4096
  * dimensions; larger requests return RV_E_INVALID.  Device buffers as in rv_index_topk_device;
  * runs on `stream` (0 = the index's stream) and returns when the results are written.  The first

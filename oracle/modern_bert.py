@@ -59,16 +59,36 @@ def weight_names(cfg: ModernBertConfig) -> list[str]:
     return names
 
 
+_Q_BLOCK = 512  # query rows per score block: keeps [block, L] f32 small at L = 8192
+
+
 def _attention(q, k, v, scale, window_half, dt):
-    """``q,k,v [L, heads, d]`` -> context ``[L, heads*d]``.  ``window_half < 0`` means global."""
+    """``q,k,v [L, heads, d]`` -> context ``[L, heads*d]``.  ``window_half < 0`` means global.
+
+    Per head, the scores ``q k^T`` are BLAS GEMMs like the reference's ``gemm_batched``
+    (``modern_bert.rs:250-263``), scaled and masked row by row (``s * scale + mask``,
+    ``driver/cpu.rs:1016-1074``), soft-maxed and multiplied by V (``:286-300``).  Rows are
+    processed in blocks of ``_Q_BLOCK`` queries so that an 8192-token chunk never materialises
+    ``[heads, L, L]``.  On windowed layers a block only forms scores for keys within
+    ``window_half`` of its rows: every other key carries the additive ``-1e9`` mask, whose
+    ``exp(s - max)`` is exactly 0 in f32, so leaving it out changes no softmax weight and adds
+    only exact zeros to ``P V``.
+    """
     L, nh, d = q.shape
-    s = np.einsum("ihd,jhd->hij", q, k, optimize=False) * dt(scale)
-    if window_half >= 0:
-        idx = np.arange(L)
-        far = np.abs(idx[:, None] - idx[None, :]) > window_half
-        s = s + np.where(far, dt(-1e9), dt(0.0))[None]
-    p = ops.softmax_rows(s)
-    ctx = np.einsum("hij,jhd->ihd", p, v, optimize=False)
+    ctx = np.empty((L, nh, d), dtype=q.dtype)
+    sc = dt(scale)
+    for h in range(nh):
+        qh = np.ascontiguousarray(q[:, h, :])
+        kh = np.ascontiguousarray(k[:, h, :])
+        vh = np.ascontiguousarray(v[:, h, :])
+        for i0 in range(0, L, _Q_BLOCK):
+            i1 = min(L, i0 + _Q_BLOCK)
+            j0, j1 = (0, L) if window_half < 0 else (max(0, i0 - window_half), min(L, i1 + window_half))
+            s = (qh[i0:i1] @ kh[j0:j1].T) * sc
+            if window_half >= 0:
+                far = np.abs(np.arange(i0, i1)[:, None] - np.arange(j0, j1)[None, :]) > window_half
+                s = s + np.where(far, dt(-1e9), dt(0.0))
+            ctx[i0:i1, h, :] = ops.softmax_rows(s) @ vh[j0:j1]
     return ctx.reshape(L, nh * d)
 
 

@@ -64,6 +64,18 @@ def scores_exact(db_bf16: np.ndarray, q_bf16: np.ndarray) -> np.ndarray:
     return acc
 
 
+def rank_exact(db: np.ndarray, query: np.ndarray, threshold: float):
+    """``SearchIndex::rank`` (``index.rs:172-186``) under the exact score definition of
+    ``topk_exact``: every row whose f64 score is ``>= threshold``, ordered by (score desc, row
+    asc).  Returns ``(idx int64 [m], score64 [m])``."""
+    dbb = ops.to_bf16(np.asarray(db, np.float32))
+    qb = ops.to_bf16(np.asarray(query, np.float32).reshape(-1))
+    s = scores_exact(dbb, qb)
+    keep = np.nonzero(s >= np.float64(np.float32(threshold)))[0]
+    order = np.lexsort((keep, -s[keep]))
+    return keep[order].astype(np.int64), s[keep[order]]
+
+
 def topk_exact(db: np.ndarray, queries: np.ndarray, k: int, threshold: float = -np.inf):
     """Reference top-k of every query: returns ``(idx int64 [nq,k], score64 [nq,k], count [nq])``.
 

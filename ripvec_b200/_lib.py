@@ -87,6 +87,7 @@ SIGNATURES = {
     "rv_index_topk": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_index_topk_device": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_index_topk_noalloc": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
+    "rv_index_rank": (C.c_int, [vp, vp, f32, i64, vp, vp, vp, C.POINTER(i64)]),
     "rv_topk_merge_device": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, f32, vp, vp, vp, vp]),
     "rv_index_build_polar": (C.c_int, [vp, vp, i32]),
     "rv_index_has_polar": (C.c_int, [vp]),

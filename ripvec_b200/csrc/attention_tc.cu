@@ -549,14 +549,15 @@ template <typename T>
 cudaError_t launch_attn_tc(const CUtensorMap& tm, void* ctx, const int2* tiles, int n_tiles,
                            int num_heads, int window_half, float scale, unsigned int* err,
                            cudaStream_t st) {
-  static bool attr_set[64] = {false};  // the attribute is per device
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+  static PerDeviceOnce attr_set;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr_set.run([&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   const int n_items = n_tiles * num_heads;
   const int slots = 2 * device_sm_count();

@@ -11,6 +11,7 @@
 // stride (conflict-free column reads), outputs staged the same way and written coalesced.
 #include "cascade.h"
 #include "common.cuh"
+#include "tmap.h"
 
 namespace rv {
 
@@ -105,14 +106,15 @@ cudaError_t cascade_rows(const __nv_bfloat16* x, int64_t n, int dim, int t, __nv
   if (dim % 2 != 0 || t % 2 != 0 || t > dim || t <= 0) return cudaErrorInvalidValue;
   const size_t smem = cascade_rows_smem(dim, t);
   if (smem > kCascadeMaxSmem) return cudaErrorInvalidValue;
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(cascade_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kCascadeMaxSmem));
-    if (e != cudaSuccess) return e;
-    attr[dev] = true;
+  static PerDeviceOnce attr;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr.run([&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(cascade_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(kCascadeMaxSmem));
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   const int64_t blocks = (n + 31) / 32;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;

@@ -19,6 +19,7 @@
 #include <utility>
 
 #include "common.cuh"
+#include "tmap.h"
 
 namespace rv {
 
@@ -464,15 +465,16 @@ cudaError_t launch_gemm_tc(const CUtensorMap& tmA, const CUtensorMap& tmB, int M
                            int b_row_offset, const Epi& epi, unsigned int* err, int num_sms,
                            cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
-  static bool attr_set[64] = {false};  // the attribute is per device
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<T, BN, Epi>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::kSmemBytes + Cfg::kEpiSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+  static PerDeviceOnce attr_set;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr_set.run([&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<T, BN, Epi>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           Cfg::kSmemBytes + Cfg::kEpiSmemBytes);
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   if (M <= 0) return cudaSuccess;
   const int tiles = ((M + kGemmBM - 1) / kGemmBM) * (N / BN);

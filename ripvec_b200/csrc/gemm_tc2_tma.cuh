@@ -327,14 +327,15 @@ template <typename T, class Epi>
 cudaError_t launch_gemm_tc2_tma(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, int M,
                                 int N, int K, const Epi& epi, unsigned int* err, int num_sms, cudaStream_t stream) {
   using Cfg = Gemm2TmaCfg;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc2_tma_kernel<T, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+  static PerDeviceOnce attr_set;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr_set.run([&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(gemm_tc2_tma_kernel<T, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           Cfg::kSmemBytes);
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   if (M <= 0) return cudaSuccess;
   if (N % Cfg::kBN != 0 || K % kGemmBK != 0) return cudaErrorInvalidValue;

@@ -17,6 +17,7 @@
 #include "dup.h"
 #include "index_impl.h"
 #include "kernels.h"
+#include "rank_all.h"
 #include "scan.h"
 #include "tmap.h"
 #include "turbo_quant.h"
@@ -393,6 +394,13 @@ void rv_index_destroy(rv_index* x) {
     x->dup_rec.release();
     x->dup_cnt.release();
     x->dup_s64.release();
+    x->rank_cand.release();
+    x->rank_cnt.release();
+    x->rank_s.release();
+    x->rank_s2.release();
+    x->rank_i.release();
+    x->rank_i2.release();
+    x->rank_tmp.release();
     if (x->stream) cudaStreamDestroy(x->stream);
   }
   delete x;
@@ -458,6 +466,87 @@ int rv_index_topk(rv_index* x, const float* queries, int32_t nq, int32_t k, floa
   IX_TRY(x, cudaStreamSynchronize(st));
   if (out_count)
     for (int q = 0; q < nq; ++q) out_count[q] = counts[q];
+  return RV_OK;
+}
+
+int rv_index_rank(rv_index* x, const float* query, float threshold, int64_t capacity, int64_t* out_idx,
+                  float* out_score, double* out_score64, int64_t* out_count) {
+  if (!x) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(x->mu);
+  if (!query || !out_count || capacity < 0 || (capacity > 0 && (!out_idx || !out_score)))
+    return ifail(x, RV_E_INVALID, "null argument");
+  *out_count = 0;
+  if (x->n == 0) return RV_OK;
+  Dev g(x->device);
+  cudaStream_t st = x->stream;
+  const int64_t n = x->n;
+  if (!x->qf.reserve(size_t(x->dim)) || !x->qb.reserve(size_t(x->dim)) || !x->rank_cnt.reserve(2) ||
+      !x->rank_s.reserve(size_t(n)) || !x->rank_i.reserve(size_t(n)) || !x->rank_s2.reserve(size_t(n)) ||
+      !x->rank_i2.reserve(size_t(n)))
+    return ifail(x, RV_E_NOMEM, "rank buffers");
+  IX_TRY(x, cudaMemcpyAsync(x->qf.p, query, sizeof(float) * x->dim, cudaMemcpyHostToDevice, st));
+  IX_TRY(x, rv::scan_round_queries(x->qf.p, x->qb.p, x->dim, st));
+  IX_TRY(x, cudaMemsetAsync(x->rank_cnt.p, 0, 2 * sizeof(unsigned long long), st));
+  // Candidates: every row when nothing can be filtered, else the rows whose f32 score reaches
+  // threshold - eps (eps: the f32 accumulation bound the top-k guard uses).
+  const bool all_rows = !(threshold > -INFINITY);
+  unsigned long long m = static_cast<unsigned long long>(n);
+  if (!all_rows) {
+    double qn2 = 0.0;
+    for (int d = 0; d < x->dim; ++d) {
+      const uint32_t bits = uint32_t(rv::f32_to_bf16_bits(query[d])) << 16;
+      float v;
+      std::memcpy(&v, &bits, 4);
+      qn2 += double(v) * v;
+    }
+    const double eps = double(x->dim) * std::ldexp(1.0, -22) * x->max_norm * std::sqrt(qn2);
+    const float lo = static_cast<float>(double(threshold) - eps - std::fabs(double(threshold)) * 1e-6);
+    if (!x->rank_cand.reserve(size_t(n))) return ifail(x, RV_E_NOMEM, "rank candidate buffer");
+    IX_TRY(x, rv::rank_filter(x->db, n, x->dim, x->qb.p, lo, x->rank_cand.p, x->rank_cnt.p, st));
+    IX_TRY(x, cudaMemcpyAsync(&m, x->rank_cnt.p, sizeof(m), cudaMemcpyDeviceToHost, st));
+    IX_TRY(x, cudaStreamSynchronize(st));
+    x->launches++;
+  }
+  IX_TRY(x, rv::rank_exact(x->db, x->dim, x->qb.p, all_rows ? nullptr : x->rank_cand.p, int64_t(m), x->base,
+                           double(threshold), x->rank_s.p, x->rank_i.p, x->rank_cnt.p + 1, st));
+  unsigned long long kept = 0;
+  IX_TRY(x, cudaMemcpyAsync(&kept, x->rank_cnt.p + 1, sizeof(kept), cudaMemcpyDeviceToHost, st));
+  unsigned int e = 0;
+  IX_TRY(x, cudaMemcpyAsync(&e, x->d_err, 4, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaStreamSynchronize(st));
+  x->launches++;
+  if (e) {
+    cudaMemset(x->d_err, 0, 4);
+    return ifail(x, RV_E_DEVICE, "rank kernel reported device error flags " + std::to_string(e));
+  }
+  *out_count = static_cast<int64_t>(kept);
+  if (kept == 0 || capacity == 0) return RV_OK;
+  size_t tmp_bytes = 0;
+  IX_TRY(x, rv::rank_sort_desc(nullptr, &tmp_bytes, x->rank_s.p, x->rank_s2.p, x->rank_i.p, x->rank_i2.p,
+                               int64_t(kept), st));
+  if (!x->rank_tmp.reserve(tmp_bytes)) return ifail(x, RV_E_NOMEM, "rank sort scratch");
+  IX_TRY(x, rv::rank_sort_desc(x->rank_tmp.p, &tmp_bytes, x->rank_s.p, x->rank_s2.p, x->rank_i.p,
+                               x->rank_i2.p, int64_t(kept), st));
+  x->launches++;
+  // Every pair comes back: equal scores arrive in no fixed order and are put in row order here,
+  // including a run that crosses the capacity.
+  std::vector<double> hs(kept);
+  std::vector<int64_t> hi(kept);
+  IX_TRY(x, cudaMemcpyAsync(hs.data(), x->rank_s2.p, sizeof(double) * kept, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaMemcpyAsync(hi.data(), x->rank_i2.p, sizeof(int64_t) * kept, cudaMemcpyDeviceToHost, st));
+  IX_TRY(x, cudaStreamSynchronize(st));
+  const size_t out_n = std::min<size_t>(kept, size_t(capacity));
+  for (size_t a = 0; a < out_n;) {
+    size_t b = a + 1;
+    while (b < kept && hs[b] == hs[a]) ++b;
+    if (b - a > 1) std::sort(hi.begin() + a, hi.begin() + b);
+    a = b;
+  }
+  for (size_t i = 0; i < out_n; ++i) {
+    out_idx[i] = hi[i];
+    out_score[i] = static_cast<float>(hs[i]);
+    if (out_score64) out_score64[i] = hs[i];
+  }
   return RV_OK;
 }
 

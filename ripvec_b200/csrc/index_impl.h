@@ -69,6 +69,13 @@ struct rv_index {
   DevBuf<int4> dup_rec;
   DevBuf<unsigned long long> dup_cnt;
   DevBuf<double> dup_s64;
+  // Full ranking (rank_all.cu): candidate rows, the two counters, (score, row) pairs and their
+  // sorted copies, and the radix sort's scratch.
+  DevBuf<int> rank_cand;
+  DevBuf<unsigned long long> rank_cnt;
+  DevBuf<double> rank_s, rank_s2;
+  DevBuf<int64_t> rank_i, rank_i2;
+  DevBuf<uint8_t> rank_tmp;
   int64_t launches = 0;
   bool filter_off = false;  // RV_SCAN_FILTER=0 at creation
 };

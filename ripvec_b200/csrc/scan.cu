@@ -17,6 +17,7 @@
 #include "common.cuh"
 #include "scan.h"
 #include "scan_sort.cuh"
+#include "tmap.h"
 
 namespace rv {
 
@@ -274,12 +275,12 @@ cudaError_t scan_select(const float* scores, int ld, int cols, int64_t row0, int
                         float* list_s, int64_t* list_i, int* list_n, cudaStream_t st) {
   const int cap = scan_cap_for(kp);
   const size_t smem = static_cast<size_t>(cap) * (8 + 4);
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr[dev] = true;
+  static PerDeviceOnce attr;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr.run([&]() -> cudaError_t {
+      return cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   select_kernel<<<nq, 256, smem, st>>>(scores, ld, cols, row0, kp, cap, list_s, list_i, list_n);
   return cudaGetLastError();
@@ -293,12 +294,12 @@ cudaError_t scan_rescore(const __nv_bfloat16* db, int64_t base, int dim, const _
   int cap = 1;
   while (cap < kp) cap <<= 1;
   const size_t smem = static_cast<size_t>(cap) * 16 + static_cast<size_t>(dim) * 4;
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaFuncSetAttribute(rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr[dev] = true;
+  static PerDeviceOnce attr;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr.run([&]() -> cudaError_t {
+      return cudaFuncSetAttribute(rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   rescore_kernel<<<nq, 256, smem, st>>>(db, base, dim, qb, list_s, list_i, list_n, kp, k, n_rows,
                                         eps_scale, threshold, out_i, out_s, out_s64, out_cnt,
@@ -313,12 +314,12 @@ cudaError_t scan_merge(const int64_t* idx_in, const double* s_in, int n_lists, i
   while (cap < n_lists * k) cap <<= 1;
   const size_t smem = static_cast<size_t>(cap) * 16;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr[dev] = true;
+  static PerDeviceOnce attr;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr.run([&]() -> cudaError_t {
+      return cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   merge_kernel<<<nq, 256, smem, st>>>(idx_in, s_in, n_lists, nq, k, threshold, idx_out, s_out,
                                       s64_out, cap);

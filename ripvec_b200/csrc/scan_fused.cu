@@ -251,16 +251,17 @@ cudaError_t scan_filter_block(const CUtensorMap& tm_rows, const CUtensorMap& tm_
   int n = 1;
   while (n < cap + kp) n <<= 1;
   const size_t smem = size_t(n) * (sizeof(int64_t) + sizeof(float));
-  static bool attr_set[64] = {false};  // set once for the largest list (kFilterMaxKp)
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    int nmax = 1;
-    while (nmax < cap + kFilterMaxKp) nmax <<= 1;
-    e = cudaFuncSetAttribute(filter_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(size_t(nmax) * (sizeof(int64_t) + sizeof(float))));
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+  static PerDeviceOnce attr_set;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr_set.run([&]() -> cudaError_t {
+      int nmax = 1;
+      while (nmax < cap + kFilterMaxKp) nmax <<= 1;
+      e = cudaFuncSetAttribute(filter_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(size_t(nmax) * (sizeof(int64_t) + sizeof(float))));
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   filter_merge_kernel<<<nq, 256, smem, st>>>(cand_s, cand_i, cand_n, cap, kp, list_s, list_i, list_n,
                                              overflow);

@@ -9,7 +9,7 @@
 // holds the rows.
 //
 // The array is part of the library image: every GPU that loads the library holds it (about
-// 4.2 MiB) until the process exits.  Its address is looked up once per device, with that device
+// 5 MiB) until the process exits.  Its address is looked up once per device, with that device
 // current, by the first call made on that device; make that first call before any stream
 // capture.  All calls share the one array and it keeps the previous call's contents, so the
 // candidate counts are cleared at the start of every call, and calls that overlap on the GPU
@@ -34,12 +34,16 @@ constexpr int kMaxK = 64;           // results per query
 constexpr int kCandidates = 128;    // candidate list width (2k rounded up, at least 128)
 constexpr int kMaxDim = 4096;       // row dimension
 constexpr int kChunkCols = 65536;   // database rows scored per GEMM launch
+constexpr int kQueryRows = 128;     // query rows of the bf16 buffer: one whole GEMM tile
 
 constexpr size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 constexpr size_t kScoresOff = 0;
 constexpr size_t kScoresBytes = size_t(kMaxQueries) * kChunkCols * sizeof(float);
 constexpr size_t kQueryOff = kScoresOff + align256(kScoresBytes);
-constexpr size_t kQueryBytes = size_t(kMaxQueries) * kMaxDim * sizeof(__nv_bfloat16);
+// The queries are read through a 128-row TMA box; the buffer holds all 128 rows (zero past nq)
+// so no box reaches past it: boxes mostly outside their tensor map (zero-filled by the copy
+// engine) make the score GEMM of a small batch about 1.5x slower.
+constexpr size_t kQueryBytes = size_t(kQueryRows) * kMaxDim * sizeof(__nv_bfloat16);
 constexpr size_t kListSOff = kQueryOff + align256(kQueryBytes);
 constexpr size_t kListSBytes = size_t(kMaxQueries) * kCandidates * sizeof(float);
 constexpr size_t kListIOff = kListSOff + align256(kListSBytes);
@@ -99,8 +103,12 @@ extern "C" int rv_index_topk_noalloc(rv_index* x, const float* queries_dev, int3
   if (!queries_dev || !out_idx_dev || !out_score_dev) return nfail(x, RV_E_INVALID, "null argument");
 
   int prev = -1;
-  cudaGetDevice(&prev);
-  if (prev != x->device) cudaSetDevice(x->device);
+  if (cudaGetDevice(&prev) != cudaSuccess) return nfail(x, RV_E_CUDA, "cudaGetDevice failed");
+  if (prev != x->device) {
+    const cudaError_t e = cudaSetDevice(x->device);
+    if (e != cudaSuccess)
+      return nfail(x, RV_E_CUDA, std::string("cudaSetDevice failed: ") + cudaGetErrorString(e));
+  }
   struct Restore {
     int dev;
     ~Restore() {
@@ -129,12 +137,14 @@ extern "C" int rv_index_topk_noalloc(rv_index* x, const float* queries_dev, int3
   } while (0)
 
   NA_TRY(rv::scan_round_queries(queries_dev, qb, int64_t(nq) * x->dim, st));
+  NA_TRY(cudaMemsetAsync(qb + size_t(nq) * x->dim, 0, size_t(kQueryRows - nq) * x->dim * sizeof(__nv_bfloat16),
+                         st));
   NA_TRY(rv::scan_init_lists(list_n, nq, st));  // the previous call's counts must not leak in
   const int kp = kCandidates;
   const int cap = rv::scan_cap_for(kp);
   if (x->n > 0) {
     CUtensorMap tq;
-    if (!rv::make_tmap_2d_16bit(&tq, qb, true, x->dim, nq, uint64_t(x->dim) * 2, 64, 128, &why))
+    if (!rv::make_tmap_2d_16bit(&tq, qb, true, x->dim, kQueryRows, uint64_t(x->dim) * 2, 64, 128, &why))
       return nfail(x, RV_E_CUDA, why);
     int64_t r0 = 0;
     int64_t chunk = std::max<int64_t>(256, (cap - kp) / 256 * 256);

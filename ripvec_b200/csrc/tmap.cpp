@@ -51,16 +51,19 @@ bool make_tmap_2d_16bit(CUtensorMap* out, const void* base, bool is_bf16, uint64
 }
 
 int device_sm_count() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
+    // Every thread that races here reads the same attribute and stores the same value.
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = n > 0 ? n : 148;
+    v = n > 0 ? n : 148;
+    cache[dev].store(v, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return v;
 }
 
 }  // namespace rv

@@ -374,14 +374,15 @@ cudaError_t launch_scan(const float* radii, const uint8_t* bins, int pairs, int6
                         int64_t valid, const float* lut, int levels, float* s, int64_t ld, int sms,
                         cudaStream_t st) {
   const size_t smem = size_t(QB) * pairs * levels * sizeof(float);
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(polar_scan_kernel<QB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kPolarMaxLutBytes));
-    if (e != cudaSuccess) return e;
-    attr[dev] = true;
+  static PerDeviceOnce attr;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr.run([&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(polar_scan_kernel<QB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(kPolarMaxLutBytes));
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   constexpr int threads = scan_threads<QB>();
   constexpr int warps_per_cta = threads / 32;
@@ -416,14 +417,15 @@ cudaError_t polar_query_tables(const float* q, int nq, int dim, const float* rt,
   if (nq <= 0) return cudaSuccess;
   if (nq > 65535) return cudaErrorInvalidValue;
   const size_t smem = size_t(dim) * sizeof(float);
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(polar_lut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         64 * 1024);
-    if (e != cudaSuccess) return e;
-    attr[dev] = true;
+  static PerDeviceOnce attr;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr.run([&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(polar_lut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           64 * 1024);
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   const dim3 grid(static_cast<unsigned>((dim / 2 + 127) / 128), static_cast<unsigned>(nq));
   polar_lut_kernel<<<grid, 128, smem, st>>>(q, dim, rt, cos_sin, levels, lut);
@@ -483,13 +485,14 @@ cudaError_t polar_select(const float* s, int64_t ld, int64_t n, int64_t row_base
   sel_collect_kernel<<<dim3(gx, nq), 256, 0, st>>>(s, ld, n, row_base, state, pre, list_i, counters, ties,
                                                     tie_cap);
   const size_t smem = size_t(tie_cap) * (sizeof(int64_t) + sizeof(double));
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    e = cudaFuncSetAttribute(sel_ties_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    attr[dev] = true;
+  static PerDeviceOnce attr;  // per-device attribute, set once under a lock
+  {
+    const cudaError_t e_once = attr.run([&]() -> cudaError_t {
+      e = cudaFuncSetAttribute(sel_ties_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (e_once != cudaSuccess) return e_once;
   }
   sel_ties_kernel<<<nq, 256, smem, st>>>(state, counters, ties, tie_cap, pre, list_i, list_n, overflow);
   return cudaGetLastError();

@@ -5,8 +5,9 @@ index.rs:76-165``) for the embedding matrix, and ``rank(query, threshold)`` to
 ``SearchIndex::rank`` (``index.rs:172-186``): a query of the wrong dimension or an empty index
 gives no results, rows scoring below ``threshold`` are dropped, results are sorted by descending
 score.  Differences, by design: rows are stored in bf16 and queries are rounded to bf16, scores
-are exact sums of the bf16 products (so equal inputs give bit-identical rankings), ties are
-ordered by row index, and one call returns at most 2048 rows per query (``top_k``).
+are exact sums of the bf16 products (so equal inputs give bit-identical rankings), and ties are
+ordered by row index.  ``rank`` returns every row at or above the threshold, like the
+reference; ``topk`` returns the best ``k <= 2048`` rows of a batch of queries.
 
 ``rank_turboquant`` mirrors ``SearchIndex::rank_turboquant`` (``index.rs:196-234``) over the
 PolarQuant codes of ``turbo_quant.rs``, built on the GPU by ``build_turboquant``.
@@ -125,17 +126,38 @@ class SearchIndex:
                                                    L.ptr(out_idx), L.ptr(out_score), L.ptr(out_score64),
                                                    stream or None))
 
+    def rank_arrays(self, query, threshold: float, capacity: int | None = None, with_f64: bool = False):
+        """Every row with exact score ``>= threshold`` ordered by (score desc, row asc), as arrays
+        ``(idx int64 [m], score f32 [m])`` (plus f64 scores), ``m = min(count, capacity)``; the
+        total count is the length when ``capacity`` is None."""
+        q = np.ascontiguousarray(query, np.float32).reshape(-1)
+        if q.shape[0] != self.hidden_dim:
+            raise ValueError(f"query has {q.shape[0]} dimensions, the index {self.hidden_dim}")
+        cap = len(self) if capacity is None else max(0, min(int(capacity), len(self)))
+        oi = np.empty(max(cap, 1), np.int64)
+        os_ = np.empty(max(cap, 1), np.float32)
+        o64 = np.empty(max(cap, 1), np.float64) if with_f64 else None
+        cnt = C.c_int64(0)
+        self._check(self._lib.rv_index_rank(self._h, q.ctypes.data, threshold, cap, oi.ctypes.data,
+                                            os_.ctypes.data, o64.ctypes.data if with_f64 else None, C.byref(cnt)))
+        m = min(int(cnt.value), cap)
+        return (oi[:m], os_[:m], o64[:m]) if with_f64 else (oi[:m], os_[:m])
+
     def rank(self, query, threshold: float, top_k: int | None = None) -> list[tuple[int, float]]:
-        """``SearchIndex::rank``: ``(row, score)`` pairs sorted by descending score, ``>= threshold``."""
+        """``SearchIndex::rank``: every ``(row, score)`` pair with score ``>= threshold``, sorted by
+        descending score (ties by row); ``top_k`` keeps only the first ``top_k``.  A query of the
+        wrong dimension or an empty index gives no results."""
         q = np.asarray(query, np.float32).reshape(-1)
         n = len(self)
         if q.shape[0] != self.hidden_dim or n == 0:
             return []
-        k = min(n, MAX_K) if top_k is None else min(top_k, n, MAX_K)
-        if k <= 0:
+        if top_k is not None and top_k <= 0:
             return []
-        oi, os_, cnt = self.topk(q[None, :], k, threshold)
-        return [(int(oi[0, i]), float(os_[0, i])) for i in range(int(cnt[0]))]
+        if top_k is not None and top_k <= MAX_K:
+            oi, os_, cnt = self.topk(q[None, :], min(top_k, n), threshold)
+            return [(int(oi[0, i]), float(os_[0, i])) for i in range(int(cnt[0]))]
+        oi, os_ = self.rank_arrays(q, threshold, top_k)
+        return list(zip(oi.tolist(), os_.astype(np.float64).tolist()))
 
     # ------------------------------------------------------------ PolarQuant ("TurboQuant")
     def build_turboquant(self, rotation: np.ndarray, bits: int = 4) -> None:

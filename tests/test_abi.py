@@ -65,7 +65,30 @@ def test_search_entry_points_reject_a_null_index_without_a_device(lib):
     assert lib.rv_index_rank_cascade(None, None, 1, 10, 0.0, None, None, None, None) == inv
     cnt = C.c_int64(-1)
     assert lib.rv_index_find_duplicates(None, 0.85, 20, None, None, None, None, C.byref(cnt)) == inv
+    assert lib.rv_index_rank(None, None, 0.0, 0, None, None, None, C.byref(cnt)) == inv
+    assert lib.rv_index_topk_noalloc(None, None, 1, 10, 0.0, None, None, None, None) == inv
+    assert lib.rv_index_topk_noalloc(None, None, 0, 10, 0.0, None, None, None, None) == inv
     assert lib.rv_index_last_error(None) == b"null index"
+
+
+def test_noalloc_argument_checks_without_a_device(lib):
+    """rv_index_topk_noalloc checks its limits before it touches a device: an empty (n = 0)
+    index needs no device copy, so it is created here on a machine without a GPU only if the
+    runtime allows it; the limit checks are then exercised, and nq = 0 returns RV_OK."""
+    import ctypes as C
+
+    h = C.c_void_p()
+    rc = lib.rv_index_create(0, None, 0, 64, _lib.RV_DTYPE_F32, 0, C.byref(h))
+    if rc != _lib.RV_OK:
+        pytest.skip("no CUDA runtime device for an index handle")
+    try:
+        assert lib.rv_index_topk_noalloc(h, None, 0, 10, 0.0, None, None, None, None) == _lib.RV_OK
+        assert lib.rv_index_topk_noalloc(h, None, 17, 10, 0.0, None, None, None, None) == _lib.RV_E_INVALID
+        assert b"at most 16 queries" in lib.rv_index_last_error(h)
+        assert lib.rv_index_topk_noalloc(h, None, 1, 65, 0.0, None, None, None, None) == _lib.RV_E_INVALID
+        assert lib.rv_index_topk_noalloc(h, None, 1, 10, 0.0, None, None, None, None) == _lib.RV_E_INVALID
+    finally:
+        lib.rv_index_destroy(h)
 
 
 def test_model_desc_layout_matches_header(tmp_path):

@@ -73,6 +73,42 @@ def test_modernbert_long_sequence_global_and_window(base_weights):
     be.close()
 
 
+@pytest.fixture(scope="module")
+def long_chunks(base_weights):
+    """Config 3's length range at its ends: one chunk of exactly max_position = 8192 tokens and one
+    of 5003, with the oracle's embeddings (computed once; about a minute of CPU)."""
+    lengths = np.array([8192, 5003], np.int32)
+    ids, cu = synth.packed_ids(lengths, MODERNBERT_BASE.vocab, seed=6)
+    ref = modern_bert.embed_batch(base_weights, modern_cfg(MODERNBERT_BASE), ids, cu)
+    return ids, cu, ref
+
+
+@pytest.mark.parametrize("dtype,bar", [("f16", COS_F16), ("bf16", COS_BF16)])
+def test_modernbert_config3_lengths_match_oracle(base_weights, long_chunks, dtype, bar):
+    """Positions 2048-8191 of the RoPE tables (built in f32 on the host, driver/cpu.rs:670-688,
+    whose rounding shows at pos ~ 8192) and global attention over 8192 keys, at the north-star
+    bars: cosine >= 0.9999 in fp16 (config 3's dtype) and >= 0.999 in bf16."""
+    ids, cu, ref = long_chunks
+    be = EmbedBackend(MODERNBERT_BASE, base_weights, dtype=dtype)
+    out = be.embed_packed(ids, cu)
+    cos = row_cosines(out, ref)
+    assert cos.min() >= bar, cos
+    be.close()
+
+
+def test_modernbert_8192_tokens_sharp_attention_fp16():
+    """The stress weights (sharp attention) at 8192 tokens in fp16: RoPE rotations at high
+    positions decide which keys win, so a wrong table entry or position cannot hide behind
+    near-uniform attention."""
+    w = synth.random_weights(MODERNBERT_BASE, seed=2, qk_std=0.07)
+    ids, cu = synth.packed_ids(np.array([8192], np.int32), MODERNBERT_BASE.vocab, seed=7)
+    ref = modern_bert.embed_batch(w, modern_cfg(MODERNBERT_BASE), ids, cu)
+    be = EmbedBackend(MODERNBERT_BASE, w, dtype="f16")
+    cos = row_cosines(be.embed_packed(ids, cu), ref)
+    be.close()
+    assert cos.min() >= COS_F16, cos
+
+
 def test_boundary_contract(tiny_modern):
     g, w = tiny_modern
     be = EmbedBackend(TINY_MODERN, w)

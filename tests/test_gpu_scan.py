@@ -131,6 +131,45 @@ def test_rank_contract(cuda_device):
     assert idx.rank(np.zeros(0, np.float32), 0.0) == []
 
 
+@pytest.mark.parametrize("threshold", [0.0, -1.0, 0.05])
+def test_rank_returns_every_row_above_threshold(cuda_device, threshold):
+    """``rank`` is not capped: 5000 rows at threshold 0.0 (about half of them), -1.0 (all 5000)
+    and 0.05, in the oracle's (score desc, row asc) order with bit-identical f64 scores; two
+    duplicated rows tie and must come out lowest row first.  MCP ``find_similar`` ranks at 0.0 and
+    pages through the result (ripvec-mcp/src/tools.rs:563-570)."""
+    db = synth.normalized_gaussian(5000, 768, seed=41)
+    db[3000] = db[12]
+    db[4999] = db[12]
+    q = synth.normalized_gaussian(1, 768, seed=42)[0]
+    ei, es = scan.rank_exact(db, q, threshold)
+    idx = SearchIndex(db)
+    oi, os_, o64 = idx.rank_arrays(q, threshold, with_f64=True)
+    np.testing.assert_array_equal(oi, ei)
+    np.testing.assert_array_equal(o64, es)
+    if threshold == -1.0:
+        assert len(oi) == 5000
+    pos = {int(r): i for i, r in enumerate(oi)}
+    if 12 in pos:
+        assert pos[3000] == pos[12] + 1 and pos[4999] == pos[12] + 2
+    res = idx.rank(q, threshold)
+    assert [r for r, _ in res] == ei.tolist()
+    # a capacity below the count returns the best ones and the total count
+    oi2, _ = idx.rank_arrays(q, threshold, capacity=7)
+    np.testing.assert_array_equal(oi2, ei[:7])
+    assert [r for r, _ in idx.rank(q, threshold, top_k=3000)] == ei[:3000].tolist()
+
+
+def test_rank_unfiltered_large_index(cuda_device):
+    """threshold = -inf scores every row without the filter pass: 300k rows, order and scores
+    against the oracle."""
+    db = synth.normalized_gaussian(300_000, 128, seed=43)
+    q = synth.normalized_gaussian(1, 128, seed=44)[0]
+    ei, es = scan.rank_exact(db, q, -np.inf)
+    oi, _, o64 = SearchIndex(db).rank_arrays(q, float("-inf"), with_f64=True)
+    np.testing.assert_array_equal(oi, ei)
+    np.testing.assert_array_equal(o64, es)
+
+
 def test_sharded_indexes_merge_on_device(cuda_device):
     import torch
 
