@@ -36,6 +36,7 @@ extern "C" {
 #define RV_E_IO -4          /* file could not be read or parsed */
 #define RV_E_DEVICE -5      /* a kernel reported an error (bounded wait expired, bad token) */
 #define RV_E_NOMEM -6       /* device allocation failed */
+#define RV_E_COMM -7        /* NCCL unavailable, a collective failed, or a rank did not answer in time */
 
 /* ---------------------------------------------------------------- model description */
 #define RV_ARCH_MODERNBERT 1  /* backend/arch/modern_bert.rs */
@@ -95,6 +96,15 @@ int rv_embed_varlen(rv_ctx* ctx, const int32_t* ids, const int32_t* cu_seqlens, 
  * cu_seqlens stays on the host (it drives the token-budget packing).  stream may be 0. */
 int rv_embed_varlen_device(rv_ctx* ctx, const int32_t* ids_dev, const int32_t* cu_seqlens_host,
                            int32_t n_seqs, void* out_dev, int32_t out_dtype, void* stream);
+
+/* embed_distributed over several backends (crates/ripvec-core/src/embed.rs:666-785): one host
+ * thread per context (each context on its own GPU, or several on one), all taking runs of
+ * consecutive chunks from one cursor in input order, each run sized to its context's token
+ * budget and embedded with rv_embed_varlen straight into out_host ([n_seqs, hidden] f32, input
+ * order).  Contexts must share the hidden size.  The first failure stops the other workers from
+ * taking new runs and is returned; its message is on the failing context (rv_last_error). */
+int rv_embed_varlen_multi(rv_ctx* const* ctxs, int32_t n_ctx, const int32_t* ids, const int32_t* cu_seqlens,
+                          int32_t n_seqs, float* out_host);
 
 int rv_max_tokens(const rv_ctx* ctx);   /* EmbedBackend::max_tokens */
 int rv_hidden_dim(const rv_ctx* ctx);
@@ -158,6 +168,39 @@ int rv_index_rank(rv_index* idx, const float* query, float threshold, int64_t ca
 int rv_topk_merge_device(int device, const int64_t* idx_in, const double* score_in,
                          int32_t n_lists, int32_t nq, int32_t k, float threshold,
                          int64_t* idx_out, float* score_out, double* score64_out, void* stream);
+
+/* ---------------------------------------------------------------- row-sharded search over GPUs
+ * A database too large for one GPU (or searched faster by several) is split into contiguous row
+ * ranges, one rv_index per GPU with rv_index_set_base giving each its first global row.  The
+ * ranks exchange their per-shard top-k lists over NCCL (one all-gather of [nq, k] rows and f64
+ * scores; NVLink / NVSwitch between the GPUs of a node) and merge them on the device.  One
+ * process or thread per GPU drives its rank.  NCCL is loaded at run time (libnccl.so.2); without
+ * it these entry points return RV_E_COMM.  No counterpart in the reference, which ranks one
+ * in-memory matrix (SearchIndex::rank, crates/ripvec-core/src/index.rs:172-186); the merged
+ * result equals rv_index_topk over the whole database. */
+typedef struct rv_comm rv_comm;
+#define RV_COMM_ID_BYTES 128
+/* Rank 0 creates the id and hands the same RV_COMM_ID_BYTES bytes to every rank (through the
+ * caller's own channel: a store, a socket, a broadcast). */
+int rv_comm_get_unique_id(uint8_t* id);
+/* Joins the communicator of `world` ranks as `rank` on CUDA device `device`.  Every wait on the
+ * communicator (this one included) gives up after timeout_ms, aborts the communicator and
+ * returns RV_E_COMM, so a rank that never joins or stops answering ends the call with an error
+ * rather than a hang. */
+int rv_comm_create(int device, const uint8_t* id, int32_t rank, int32_t world, int32_t timeout_ms,
+                   rv_comm** out);
+void rv_comm_destroy(rv_comm* comm);
+const char* rv_comm_last_error(const rv_comm* comm);
+int rv_comm_rank(const rv_comm* comm);
+int rv_comm_world(const rv_comm* comm);
+/* The exact global top k of the queries over every rank's shard: this shard's best k
+ * (rv_index_topk_device), the all-gather of every rank's lists, and the device merge by
+ * (score desc, row asc).  Every rank passes the same queries (device f32 [nq, dim]) and receives
+ * the same [nq, k] results (device buffers, as rv_index_topk_device); every rank must make the
+ * same calls in the same order.  world * k <= 8192.  Returns when the results are written. */
+int rv_index_topk_sharded(rv_index* idx, rv_comm* comm, const float* queries_dev, int32_t nq, int32_t k,
+                          float threshold, int64_t* out_idx_dev, float* out_score_dev,
+                          double* out_score64_dev, void* stream);
 
 /* The same exact top-k as rv_index_topk_device for callers that cannot allocate device memory
  * (a host whose allocator or memory pool owns the whole device budget, or a serving thread that

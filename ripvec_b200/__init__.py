@@ -6,8 +6,8 @@ The compute path is ``librv_b200.so`` (hand-written CUDA for sm_100a behind a C 
 (``index.py``).
 """
 
-from .backend import EmbedBackend, Encoding, load_backend, pack_encodings  # noqa: F401
+from .backend import EmbedBackend, Encoding, embed_distributed, load_backend, pack_encodings  # noqa: F401
 from .synth import BERT_SMALL, MODERNBERT_BASE, ModelSpec  # noqa: F401
 
-__all__ = ["EmbedBackend", "Encoding", "load_backend", "pack_encodings", "ModelSpec", "MODERNBERT_BASE",
+__all__ = ["EmbedBackend", "Encoding", "embed_distributed", "load_backend", "pack_encodings", "ModelSpec", "MODERNBERT_BASE",
            "BERT_SMALL"]

@@ -18,6 +18,8 @@ RV_E_NOT_READY = -3
 RV_E_IO = -4
 RV_E_DEVICE = -5
 RV_E_NOMEM = -6
+RV_E_COMM = -7
+RV_COMM_ID_BYTES = 128
 
 RV_ARCH_MODERNBERT = 1
 RV_ARCH_CLASSICBERT = 2
@@ -70,6 +72,7 @@ SIGNATURES = {
     "rv_finalize": (C.c_int, [vp]),
     "rv_embed_varlen": (C.c_int, [vp, vp, vp, i32, vp]),
     "rv_embed_varlen_device": (C.c_int, [vp, vp, vp, i32, vp, i32, vp]),
+    "rv_embed_varlen_multi": (C.c_int, [vp, i32, vp, vp, i32, vp]),
     "rv_max_tokens": (C.c_int, [vp]),
     "rv_hidden_dim": (C.c_int, [vp]),
     "rv_name": (C.c_char_p, [vp]),
@@ -88,6 +91,13 @@ SIGNATURES = {
     "rv_index_topk_device": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_index_topk_noalloc": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_index_rank": (C.c_int, [vp, vp, f32, i64, vp, vp, vp, C.POINTER(i64)]),
+    "rv_comm_get_unique_id": (C.c_int, [vp]),
+    "rv_comm_create": (C.c_int, [C.c_int, vp, i32, i32, i32, C.POINTER(vp)]),
+    "rv_comm_destroy": (None, [vp]),
+    "rv_comm_last_error": (C.c_char_p, [vp]),
+    "rv_comm_rank": (C.c_int, [vp]),
+    "rv_comm_world": (C.c_int, [vp]),
+    "rv_index_topk_sharded": (C.c_int, [vp, vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_topk_merge_device": (C.c_int, [C.c_int, vp, vp, i32, i32, i32, f32, vp, vp, vp, vp]),
     "rv_index_build_polar": (C.c_int, [vp, vp, i32]),
     "rv_index_has_polar": (C.c_int, [vp]),

@@ -147,6 +147,29 @@ class EmbedBackend:
         return int(self._lib.rv_kernel_launches(self._h))
 
 
+def embed_distributed(backends: Sequence[EmbedBackend], ids: np.ndarray, cu_seqlens: np.ndarray,
+                      out: np.ndarray | None = None) -> np.ndarray:
+    """``embed_distributed`` over several backends (``embed.rs:666-785``) through
+    ``rv_embed_varlen_multi``: one host thread per backend, runs of consecutive chunks taken from
+    one cursor, results in input order; the first failure is raised."""
+    if not backends:
+        raise ValueError("no backends")
+    ids = np.ascontiguousarray(ids, np.int32)
+    cu = np.ascontiguousarray(cu_seqlens, np.int32)
+    n = len(cu) - 1
+    hidden = backends[0].spec.hidden
+    if out is None:
+        out = np.empty((max(n, 0), hidden), np.float32)
+    handles = (C.c_void_p * len(backends))(*[b._h.value for b in backends])
+    lib = L.lib()
+    rc = lib.rv_embed_varlen_multi(handles, len(backends), ids.ctypes.data if ids.size else None, cu.ctypes.data,
+                                   n, out.ctypes.data)
+    if rc != L.RV_OK:
+        msgs = [lib.rv_last_error(b._h).decode() for b in backends]
+        raise L.RvError(rc, "; ".join(m for m in msgs if m) or "rv_embed_varlen_multi failed")
+    return out
+
+
 def load_backend(spec: ModelSpec, weights: dict | None = None, **kw) -> EmbedBackend:
     """``backend::load_backend`` for this library (CUDA only; no CPU fallback)."""
     return EmbedBackend(spec, weights, **kw)

@@ -14,6 +14,8 @@
 #include <fstream>
 #include <memory>
 #include <new>
+#include <thread>
+#include <vector>
 
 #include "engine.h"
 #include "tmap.h"
@@ -852,6 +854,64 @@ int rv_embed_varlen_device(rv_ctx* c, const int32_t* ids_dev, const int32_t* cu,
   rc = check_device_error(c);
   collect_marks(c);
   return rc;
+}
+
+int rv_embed_varlen_multi(rv_ctx* const* ctxs, int32_t n_ctx, const int32_t* ids, const int32_t* cu, int32_t n,
+                          float* out_host) {
+  if (!ctxs || n_ctx <= 0 || n < 0 || (n > 0 && (!cu || !out_host))) return RV_E_INVALID;
+  for (int32_t i = 0; i < n_ctx; ++i)
+    if (!ctxs[i] || ctxs[i]->d.hidden != ctxs[0]->d.hidden) return RV_E_INVALID;
+  if (n == 0) return RV_OK;
+  if (cu[0] != 0) return RV_E_INVALID;
+  for (int32_t b = 0; b < n; ++b)
+    if (cu[b + 1] < cu[b]) return RV_E_INVALID;
+  if (cu[n] > 0 && !ids) return RV_E_INVALID;
+  const int H = ctxs[0]->d.hidden;
+  // Work is handed out in input order from one cursor: each worker takes the next run of
+  // consecutive chunks that fills its context's token budget, embeds it with rv_embed_varlen
+  // straight into its rows of out_host, and comes back for more, so a faster device takes more
+  // runs.  The first failure stops the others from taking new runs.
+  std::mutex mu;
+  int32_t next = 0;
+  int first_rc = RV_OK;
+  int first_ctx = n_ctx;
+  auto worker = [&](int32_t wi) {
+    rv_ctx* c = ctxs[wi];
+    const int64_t budget = std::max<int64_t>(1, c->t_max > 0 ? c->t_max : 262144);
+    std::vector<int32_t> lcu;
+    for (;;) {
+      int32_t b0, b1;
+      {
+        std::lock_guard<std::mutex> lk(mu);
+        if (first_rc != RV_OK || next >= n) return;
+        b0 = next;
+        b1 = b0 + 1;  // at least one chunk, even one longer than the budget (rv_embed_varlen checks it)
+        while (b1 < n && int64_t(cu[b1 + 1]) - cu[b0] <= budget) ++b1;
+        next = b1;
+      }
+      lcu.resize(size_t(b1 - b0) + 1);
+      for (int32_t b = b0; b <= b1; ++b) lcu[b - b0] = cu[b] - cu[b0];
+      const int rc = rv_embed_varlen(c, ids ? ids + cu[b0] : nullptr, lcu.data(), b1 - b0,
+                                     out_host + size_t(b0) * H);
+      if (rc != RV_OK) {
+        std::lock_guard<std::mutex> lk(mu);
+        if (first_rc == RV_OK || wi < first_ctx) {
+          first_rc = rc;
+          first_ctx = wi;
+        }
+        return;
+      }
+    }
+  };
+  if (n_ctx == 1) {
+    worker(0);
+  } else {
+    std::vector<std::thread> ts;
+    ts.reserve(size_t(n_ctx));
+    for (int32_t i = 0; i < n_ctx; ++i) ts.emplace_back(worker, i);
+    for (auto& t : ts) t.join();
+  }
+  return first_rc;
 }
 
 int rv_max_tokens(const rv_ctx* c) { return c ? c->d.max_position : 0; }

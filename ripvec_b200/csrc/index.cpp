@@ -14,6 +14,7 @@
 #include "../../include/ripvec_b200.h"
 #include "engine.h"
 #include "cascade.h"
+#include "comm_impl.h"
 #include "dup.h"
 #include "index_impl.h"
 #include "kernels.h"
@@ -429,6 +430,52 @@ int rv_index_topk_device(rv_index* x, const float* q_dev, int32_t nq, int32_t k,
     IX_TRY(x, cudaStreamWaitEvent(x->stream, ev, 0));
   }
   int rc = topk_device(x, q_dev, nq, k, threshold, out_i, out_s, out_s64, nullptr);
+  if (ev) {
+    if (rc == RV_OK) {
+      cudaEventRecord(ev, x->stream);
+      cudaStreamWaitEvent(user, ev, 0);
+    }
+    cudaEventDestroy(ev);
+  }
+  return rc;
+}
+
+int rv_index_topk_sharded(rv_index* x, rv_comm* comm, const float* q_dev, int32_t nq, int32_t k,
+                          float threshold, int64_t* out_i, float* out_s, double* out_s64, void* stream) {
+  if (!x) return RV_E_INVALID;
+  if (!comm) return ifail(x, RV_E_INVALID, "null communicator");
+  std::lock_guard<std::mutex> lk(x->mu);
+  std::lock_guard<std::mutex> lkc(comm->mu);
+  if (nq < 0 || (nq > 0 && (!q_dev || !out_i || !out_s))) return ifail(x, RV_E_INVALID, "null argument");
+  if (comm->device != x->device) return ifail(x, RV_E_INVALID, "index and communicator are on different devices");
+  if (nq == 0) return RV_OK;
+  if (k <= 0 || k > 2048) return ifail(x, RV_E_INVALID, "k must be in [1, 2048]");
+  if (int64_t(comm->world) * k > 8192)
+    return ifail(x, RV_E_INVALID, "world * k must be at most 8192 (the merge keeps every list in shared memory)");
+  Dev g(x->device);
+  cudaStream_t user = static_cast<cudaStream_t>(stream);
+  cudaEvent_t ev = nullptr;
+  if (user) {
+    IX_TRY(x, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    IX_TRY(x, cudaEventRecord(ev, user));
+    IX_TRY(x, cudaStreamWaitEvent(x->stream, ev, 0));
+  }
+  // This shard's best k (global row numbers through the index's base), then every rank's lists
+  // on every rank, then the device merge by (score desc, row asc): the exact global top k, since
+  // the f64 scores are exact and every shard's list holds all of its rows that can be in it.
+  const size_t nk = size_t(nq) * k;
+  int rc = RV_OK;
+  if (!x->oi.reserve(nk) || !x->os.reserve(nk) || !x->os64.reserve(nk)) rc = ifail(x, RV_E_NOMEM, "shard lists");
+  if (!rc) rc = topk_device(x, q_dev, nq, k, threshold, x->oi.p, x->os.p, x->os64.p, nullptr);
+  int64_t* gi = nullptr;
+  double* gs = nullptr;
+  if (!rc) {
+    rc = rv_comm_allgather_lists(comm, x->oi.p, x->os64.p, nk, &gi, &gs, x->stream);
+    if (rc) x->err = comm->err;
+  }
+  if (!rc && rv::scan_merge(gi, gs, comm->world, nq, k, threshold, out_i, out_s, out_s64, x->stream) != cudaSuccess)
+    rc = ifail(x, RV_E_CUDA, "top-k merge launch failed");
+  if (!rc) x->launches += 2;
   if (ev) {
     if (rc == RV_OK) {
       cudaEventRecord(ev, x->stream);

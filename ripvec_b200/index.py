@@ -276,6 +276,58 @@ class SearchIndex:
         return [(int(x), int(y), float(z)) for x, y, z in zip(a, b, s)]
 
 
+class ShardComm:
+    """NCCL communicator of a row-sharded search (``rv_comm_*``): rank ``rank`` of ``world`` on
+    CUDA device ``device``.  ``unique_id`` (``RV_COMM_ID_BYTES`` bytes from ``new_unique_id`` on
+    rank 0) reaches every rank through the caller's own channel.  Every wait gives up after
+    ``timeout_ms`` with an error instead of hanging."""
+
+    def __init__(self, unique_id: bytes, rank: int, world: int, device: int = 0, timeout_ms: int = 60000):
+        self._lib = L.lib()
+        if len(unique_id) != L.RV_COMM_ID_BYTES:
+            raise ValueError(f"unique id must be {L.RV_COMM_ID_BYTES} bytes")
+        buf = (C.c_uint8 * L.RV_COMM_ID_BYTES).from_buffer_copy(unique_id)
+        h = C.c_void_p()
+        rc = self._lib.rv_comm_create(device, buf, rank, world, timeout_ms, C.byref(h))
+        if rc != L.RV_OK:
+            raise L.RvError(rc, "rv_comm_create failed (NCCL missing, bad id, or a rank did not join in time)")
+        self._h = h
+        self.rank, self.world, self.device = rank, world, device
+
+    @staticmethod
+    def new_unique_id() -> bytes:
+        buf = (C.c_uint8 * L.RV_COMM_ID_BYTES)()
+        rc = L.lib().rv_comm_get_unique_id(buf)
+        if rc != L.RV_OK:
+            raise L.RvError(rc, "rv_comm_get_unique_id failed (NCCL could not be loaded)")
+        return bytes(buf)
+
+    def last_error(self) -> str:
+        return self._lib.rv_comm_last_error(self._h).decode()
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.rv_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def topk_sharded(index: "SearchIndex", comm: ShardComm, queries_dev, k: int, out_idx, out_score,
+                 out_score64=None, threshold: float = float("-inf"), stream: int = 0) -> None:
+    """``rv_index_topk_sharded``: the global top ``k`` over every rank's shard (same queries on
+    every rank, same results on every rank; device tensors)."""
+    nq = queries_dev.shape[0]
+    rc = L.lib().rv_index_topk_sharded(index._h, comm._h, L.ptr(queries_dev), nq, k, threshold, L.ptr(out_idx),
+                                       L.ptr(out_score), L.ptr(out_score64), stream or None)
+    if rc != L.RV_OK:
+        raise L.RvError(rc, index._lib.rv_index_last_error(index._h).decode())
+
+
 def merge_topk_device(idx_lists, score64_lists, k: int, threshold: float = float("-inf"), device: int = 0,
                       stream: int = 0):
     """Merges per-shard device results ``[n_lists, nq, k]`` (int64 idx, f64 scores) on the GPU;
