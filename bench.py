@@ -19,12 +19,18 @@ every rank embeds its own 4096 chunks).
   stream over the timed region; algorithmic FLOPs 2*M*N*K per launch.
 * ``cpu_baseline``: the numpy port of the reference fp32 CPU path (``oracle/``) on a bounded
   sample of the same chunks, rank 0, N = 1.
+* ``parity``: min / p50 cosine of 16 chunks of the timed output against that port.
+* ``sweep_tokens_per_s`` (config 4, strong scaling): 100k log-normal chunks sharded over the
+  ranks by token count, max over ranks of the device time.
+* ``scan_step_ms`` (config 5): one 1024-query top-100 step over a 10M x 768 bf16 database
+  row-sharded over the ranks, through ``rv_index_topk_sharded`` (the library's NCCL all-gather
+  of the per-shard lists and device merge).
 
 ``--impl reference`` times that CPU port as the reference arm (rank 0 only).  Other workloads:
 ``--workload long`` (config 3, fp16, 512 chunks of 2048..8192 tokens), ``--workload sweep``
 (config 4, 1M log-normal chunks sharded by token count), ``--workload scan`` (config 5, exact
 top-100 over a 10M x 768 bf16 database, 1024 queries by default or a list such as
-``--queries 1,16,64,128``, per-shard results merged after one NCCL all-gather),
+``--queries 1,16,64,128``; with several ranks through ``rv_index_topk_sharded``),
 ``--workload turboquant`` (``rank_turboquant`` over 4-bit PolarQuant codes of the same database),
 ``--workload duplicates`` (``find_duplicates`` over 200k x 768 rows: every pair scored),
 ``--workload cascade`` (``rank_cascade`` over the 10M x 768 database truncated to 256 dimensions),
@@ -70,6 +76,10 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the 16-chunk oracle check of the timed output")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the sweep (config 4) and sharded-scan (config 5) keys of the encoder line")
+    ap.add_argument("--sweep-chunks", type=int, default=100_000,
+                    help="chunks of the strong-scaling sweep key (log-normal lengths, all ranks together)")
     return ap.parse_args()
 
 
@@ -328,6 +338,101 @@ def traffic_per_flop():
     return d["dram_bytes"] / d["flops"]
 
 
+def make_shard_comm(dist, rank, world, local):
+    """The library's NCCL communicator for the sharded search: rank 0's unique id reaches every
+    rank through the harness's process group (the caller's own channel, as the C ABI expects)."""
+    import torch
+
+    from ripvec_b200 import _lib as L
+    from ripvec_b200.index import ShardComm
+
+    if dist is None:
+        uid = ShardComm.new_unique_id()
+    else:
+        t = torch.zeros(L.RV_COMM_ID_BYTES, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            t.copy_(torch.frombuffer(bytearray(ShardComm.new_unique_id()), dtype=torch.uint8))
+        dist.broadcast(t, 0)
+        uid = bytes(t.cpu().numpy().tobytes())
+    return ShardComm(uid, rank, world, device=local, timeout_ms=120000)
+
+
+def device_database_shard(torch, lo, hi, dim, seed):
+    """Rows [lo, hi) of the synthetic database: Gaussian, L2-normalised, bf16, made on the device
+    in blocks (seeded per rank)."""
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    shard = torch.empty(hi - lo, dim, device="cuda", dtype=torch.bfloat16)
+    for s in range(0, hi - lo, 1 << 20):
+        e = min(hi - lo, s + (1 << 20))
+        x = torch.randn(e - s, dim, device="cuda", generator=gen)
+        shard[s:e] = (x / x.norm(dim=1, keepdim=True)).to(torch.bfloat16)
+    return shard
+
+
+def sweep_extra(args, torch, be, spec, barrier, max_over_ranks, rank, world, stream):
+    """Config 4 as a strong-scaling key: a fixed set of log-normal chunks (median 180, sigma 0.8,
+    clip [16, 1024]) sharded over the ranks by token count; each rank embeds its shard with ids
+    in HBM; time = max over ranks of the CUDA-event time of the whole shard."""
+    from ripvec_b200 import synth
+
+    n_total = args.sweep_chunks
+    all_len, mine = sweep_shard(rank, world, n_total)
+    lengths = all_len[mine]
+    ids, cu = synth.packed_ids(lengths, spec.vocab, seed=5000 + rank)
+    ids_dev = torch.from_numpy(ids).cuda()
+    out = torch.empty(len(lengths), spec.hidden, device="cuda", dtype=torch.float32)
+    w = min(len(lengths), 2000)
+    be.embed_device(ids_dev, cu[:w + 1], out, stream=stream.cuda_stream)  # warm-up on a prefix
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    be.embed_device(ids_dev, cu, out, stream=stream.cuda_stream)
+    b.record(stream)
+    barrier()
+    ms = max_over_ranks(a.elapsed_time(b))
+    total_tokens = int(all_len.sum())
+    return {"tokens_per_s": total_tokens / (ms / 1e3), "ms": ms, "chunks": n_total, "tokens": total_tokens,
+            "scaling": "strong", "sharding": "shard_by_tokens (longest first to the rank with the fewest tokens)",
+            "lengths": "log-normal median 180 sigma 0.8 clip [16,1024]",
+            "rank0_chunks": int(len(lengths)), "rank0_tokens": int(cu[-1])}
+
+
+def scan_extra(args, torch, dist, rank, world, local, barrier, max_over_ranks, stream):
+    """Config 5 as a key of the encoder line: one 1024-query top-100 step over a 10M x 768 bf16
+    database row-sharded across the ranks, through rv_index_topk_sharded (shard top-k, one NCCL
+    all-gather inside the library, device merge).  Time = max over ranks of CUDA events."""
+    from ripvec_b200 import shard as shard_mod
+    from ripvec_b200 import synth
+    from ripvec_b200.index import SearchIndex, topk_sharded
+
+    n_rows, dim, nq, k = args.scan_rows, 768, 1024, 100
+    lo, hi = shard_mod.row_ranges(n_rows, world)[rank]
+    db = device_database_shard(torch, lo, hi, dim, 100 + rank)
+    idx = SearchIndex(db, device=local, base=lo)
+    del db
+    comm = make_shard_comm(dist, rank, world, local)
+    q = torch.from_numpy(synth.normalized_gaussian(nq, dim, seed=99)).cuda()
+    oi = torch.empty(nq, k, dtype=torch.int64, device="cuda")
+    os_ = torch.empty(nq, k, dtype=torch.float32, device="cuda")
+    o64 = torch.empty(nq, k, dtype=torch.float64, device="cuda")
+    steps = 5
+    for _ in range(3):
+        topk_sharded(idx, comm, q, k, oi, os_, o64, stream=stream.cuda_stream)
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for s in range(steps):
+        evs[s][0].record(stream)
+        topk_sharded(idx, comm, q, k, oi, os_, o64, stream=stream.cuda_stream)
+        evs[s][1].record(stream)
+    barrier()
+    ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / steps)
+    comm.close()
+    idx.close()
+    return {"step_ms": ms, "queries_per_s": nq / (ms / 1e3), "rows": n_rows, "dim": dim, "queries": nq, "k": k,
+            "rows_per_rank": hi - lo, "entry_point": "rv_index_topk_sharded (NCCL all-gather + device merge)",
+            "steps": steps, "warmup": 3}
+
+
 def run_encoder(args):
     import torch
 
@@ -480,6 +585,11 @@ def run_encoder(args):
         cpu = {"value": r, "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"first {nc} chunks of the workload ({tok} tokens, {dt:.1f} s), numpy fp32 port of the reference CPU path"}
 
+    sweep = scan = None
+    if args.workload == "encoder" and not args.no_extras:
+        sweep = sweep_extra(args, torch, be, spec, barrier, max_over_ranks, rank, world, stream)
+        scan = scan_extra(args, torch, dist, rank, world, local, barrier, max_over_ranks, stream)
+
     if dist is not None:
         dist.barrier()
     if rank == 0:
@@ -495,6 +605,12 @@ def run_encoder(args):
                 "parity": parity, "clocks": clocks, "kernels": kernels,
                 "whole_step_tflops": whole_flops / (total_ms / args.steps / 1e3) / 1e12,
                 "attention_tflops": (att["flops"] / (att["ms"] / 1e3) / 1e12) if att["ms"] else None}
+        if sweep is not None:
+            line["sweep_tokens_per_s"] = sweep["tokens_per_s"]
+            line["sweep"] = sweep
+        if scan is not None:
+            line["scan_step_ms"] = scan["step_ms"]
+            line["scan"] = scan
         print(json.dumps(line), flush=True)
     be.close()
     if dist is not None:
@@ -505,7 +621,7 @@ def run_scan(args):
     import torch
 
     from ripvec_b200 import synth
-    from ripvec_b200.index import SearchIndex, merge_topk_device
+    from ripvec_b200.index import SearchIndex
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -521,40 +637,38 @@ def run_scan(args):
 
     lo, hi = shard_mod.row_ranges(n_rows, world)[rank]
     # shard rows generated on the device in blocks (normalised Gaussian, rounded to bf16 by the index)
-    gen = torch.Generator(device="cuda").manual_seed(100 + rank)
-    shard = torch.empty(hi - lo, dim, device="cuda", dtype=torch.bfloat16)
-    for s in range(0, hi - lo, 1 << 20):
-        e = min(hi - lo, s + (1 << 20))
-        x = torch.randn(e - s, dim, device="cuda", generator=gen)
-        shard[s:e] = (x / x.norm(dim=1, keepdim=True)).to(torch.bfloat16)
+    shard = device_database_shard(torch, lo, hi, dim, 100 + rank)
     idx = SearchIndex(shard, device=local, base=lo)
     del shard
+    comm = make_shard_comm(dist, rank, world, local) if world > 1 else None
     stream = torch.cuda.current_stream()
     # The database shard (15.4 GB at 10M rows on one GPU) is larger than L2, so every step
     # streams it from HBM: no flush is needed between steps.
     for nq in [int(v) for v in str(args.queries).split(",")]:
-        scan_line(args, torch, dist, idx, merge_topk_device, synth, stream, rank, world, local,
-                  n_rows, dim, nq, k)
+        scan_line(args, torch, dist, idx, comm, synth, stream, rank, world, local, n_rows, dim, nq, k)
+    if comm is not None:
+        comm.close()
     idx.close()
     if dist is not None:
         dist.destroy_process_group()
 
 
-def scan_line(args, torch, dist, idx, merge_topk_device, synth, stream, rank, world, local, n_rows, dim, nq, k):
-    """Times ``args.steps`` exact top-k steps of ``nq`` queries and prints one JSON line (rank 0)."""
+def scan_line(args, torch, dist, idx, comm, synth, stream, rank, world, local, n_rows, dim, nq, k):
+    """Times ``args.steps`` exact top-k steps of ``nq`` queries and prints one JSON line (rank 0).
+    With several ranks a step is ``rv_index_topk_sharded``: the shard's top-k, the library's
+    NCCL all-gather of the lists and the device merge."""
+    from ripvec_b200.index import topk_sharded
+
     q = torch.from_numpy(synth.normalized_gaussian(nq, dim, seed=99)).cuda()
     oi = torch.empty(nq, k, dtype=torch.int64, device="cuda")
     os_ = torch.empty(nq, k, dtype=torch.float32, device="cuda")
     o64 = torch.empty(nq, k, dtype=torch.float64, device="cuda")
 
     def step():
-        idx.topk_device(q, k, oi, os_, o64, stream=stream.cuda_stream)
-        if dist is not None:
-            gi = [torch.empty_like(oi) for _ in range(world)]
-            gs = [torch.empty_like(o64) for _ in range(world)]
-            dist.all_gather(gi, oi)
-            dist.all_gather(gs, o64)
-            merge_topk_device(torch.stack(gi), torch.stack(gs), k, device=local, stream=stream.cuda_stream)
+        if comm is None:
+            idx.topk_device(q, k, oi, os_, o64, stream=stream.cuda_stream)
+        else:
+            topk_sharded(idx, comm, q, k, oi, os_, o64, stream=stream.cuda_stream)
 
     for _ in range(args.warmup):
         step()
