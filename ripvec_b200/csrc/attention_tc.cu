@@ -1,30 +1,37 @@
 // Varlen attention on the 5th-generation tensor cores (head_dim 64, bf16 or f16).
 //
 // Work item = (128-query tile of one sequence, head); the host lists the tiles as
-// {sequence start, length | first query << 16} records.  The kernel is persistent: two CTAs per
-// SM each walk the items blockIdx.x, blockIdx.x + gridDim.x, ... (head-major, so the items in
-// flight share their sequences' K/V in L2), and every ring below runs across item boundaries,
-// so the next item's Q and K/V load while the current one finishes.  Warp roles (320 threads):
-//   warp 0      TMA producers: lane 0 loads Q per item (2 buffers) and K tiles (3-deep ring),
-//               lane 1 loads V tiles (2-deep ring), 64 keys per tile,
+// {sequence start, length | first query << 16} records, longest sequences first.  The kernel is
+// persistent: two CTAs per SM each walk the items blockIdx.x, blockIdx.x + gridDim.x, ...
+// (head-major, so the items in flight share their sequences' K/V in L2), and every ring below
+// runs across item boundaries, so the next item's Q and K/V load while the current one finishes.
+// Warp roles (320 threads):
+//   warp 0      TMA producers: lane 0 loads Q per item (2 buffers) and K tiles (4-deep ring),
+//               lane 1 loads V tiles (3-deep ring), 64 keys per tile,
 //   warp 1      TMEM owner and single-thread tcgen05.mma issuer,
-//   warps 2..9  softmax: warps w and w + 4 share TMEM lane quadrant w % 4 (query rows) and take
-//               32 keys each of every tile.
+//   warps 2..5  softmax: warp w owns TMEM lane quadrant w % 4 (32 query rows, one per thread)
+//               and all 64 keys of every tile.
 // Per key tile g (counted across items):
-//   S[g&1] = Q K^T      tcgen05.mma M=128 N=64 K=64 into TMEM, issued two tiles ahead,
-//   softmax             each thread reads its 32 scores with tcgen05.ld, masks keys past the
-//                       sequence end and, on sliding-window layers, keys with |i - j| > w/2
+//   S[g%3] = Q K^T      tcgen05.mma M=128 N=64 K=64 into TMEM, issued three tiles ahead, so the
+//                       softmax warps find the next tile's scores ready when they finish one and
+//                       the MMA round trip stays off their critical path,
+//   softmax             each thread reads its row's 64 scores with tcgen05.ld, masks keys past
+//                       the sequence end and, on sliding-window layers, keys with |i - j| > w/2
 //                       (32-key halves that no row of the warp can see skip the exponentials);
-//                       the two warps of a row exchange their maxima; P = exp2(s - m) is
-//                       written as packed 16-bit pairs over S[g&1] in TMEM (tcgen05.st),
+//                       P = exp2(s - m) is
+//                       written as packed 16-bit pairs over S[g%3] in TMEM (tcgen05.st),
 //   O += P V            tcgen05.mma M=128 N=64 K=64 with P (A) read from TMEM and V as an
-//                       MN-major shared-memory operand, into the item's TMEM accumulator; the
+//                       MN-major shared-memory operand, into the TMEM accumulator O; the
 //                       reference max m moves only when a row's max grows by more than 2^8
 //                       (then the row's O is rescaled in TMEM), and the item's context rows are
-//                       written after the next item's first tile.
+//                       read out of O after the next item's first P is written, before that
+//                       item's first P V overwrites O.
 // Reference semantics: backend/arch/modern_bert.rs:250-322 and driver/cpu.rs:1016-1074 (scores *
 // 1/sqrt(d), additive -1e9 masks for padding and |i-j| > window/2, max-subtracted softmax, P V);
 // masked keys get weight 0 exactly, as exp(-1e9 - max) does in f32.
+#include <algorithm>
+#include <vector>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tmap.h"
@@ -36,19 +43,21 @@ namespace {
 constexpr int kBQ = 128;       // queries per item
 constexpr int kBKV = 64;       // keys per tile
 constexpr int kD = 64;         // head dim
-// K is on the critical path (S of tile g + 2 needs it) and is loaded kKStages tiles ahead; V
-// is needed only when P V is issued.
-constexpr int kKStages = 3;
-constexpr int kVStages = 2;
+// Score buffers in TMEM: S of tile g + 3 is issued once P V of tile g (which reads P out of the
+// same columns) has been issued.  K is on the critical path (S needs it kSBufs tiles ahead of
+// the softmax) and is loaded kKStages tiles ahead; V is needed only when P V is issued.
+constexpr int kSBufs = 3;
+constexpr int kKStages = 4;
+constexpr int kVStages = 3;
 constexpr int kQBytes = kBQ * kD * 2;    // 16 KB
 constexpr int kKVBytes = kBKV * kD * 2;  // 8 KB
-constexpr int kTmemCols = 256;           // S[2] at columns 0, 64; O[2] at 128, 192
-constexpr int kThreads = 320;  // producer, MMA issuer, 8 softmax warps
-// Row-max / row-sum exchange between the two softmax warps of a row: max [2 tiles][2 halves][128]
-// and sum [2 items][2 halves][128] floats.
-constexpr int kXBytes = (2 * 2 * kBQ + 2 * 2 * kBQ) * 4;
-// 78 KB: two CTAs fit an SM; TMEM (256 columns per CTA) keeps it at two.
-constexpr int kSmem = 1024 + 2 * kQBytes + (kKStages + kVStages) * kKVBytes + kXBytes + 512;
+constexpr int kOCol = kSBufs * kBKV;     // O after the score buffers
+constexpr int kTmemCols = 256;           // S[3] at columns 0, 64, 128; O at 192
+static_assert(kOCol + kD <= kTmemCols, "TMEM layout");
+constexpr int kThreads = 192;  // producer, MMA issuer, 4 softmax warps
+constexpr int kSoftmaxWarps = 4;
+// 90 KB: two CTAs fit an SM; TMEM (256 columns per CTA) keeps it at two.
+constexpr int kSmem = 1024 + 2 * kQBytes + (kKStages + kVStages) * kKVBytes + 512;
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -80,21 +89,6 @@ __device__ __forceinline__ bool wait_done(uint64_t* bar, uint32_t parity) {
 
 __host__ __device__ constexpr uint32_t idesc_f16_bmn(int M, int N, bool is_bf16) {
   return idesc_f16(M, N, is_bf16) | (1u << 16);  // B operand MN-major
-}
-
-// Barrier of the two softmax warps of a row (named barrier `id`, 64 threads) that also ORs a
-// flag over them, so a wait that failed in either warp ends both at the same point.
-__device__ __forceinline__ bool pair_any(int id, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.b32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, %2, 64, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}\n"
-      : "=r"(r)
-      : "r"(static_cast<int>(pred)), "r"(id)
-      : "memory");
-  return r != 0;
 }
 
 // Class of 32 keys [kb, kb + 31] for the 32 queries [qa, qb] of one warp: 0 = visible to none of
@@ -217,20 +211,18 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
   uint8_t* sQ = smem;                        // [2] x 16 KB
   uint8_t* sK = sQ + 2 * kQBytes;            // [kKStages] x 8 KB
   uint8_t* sV = sK + kKStages * kKVBytes;    // [kVStages] x 8 KB
-  float* xmax = reinterpret_cast<float*>(sV + kVStages * kKVBytes);  // [2][2][kBQ]
-  float* xsum = xmax + 2 * 2 * kBQ;                           // [2][2][kBQ]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(xsum + 2 * 2 * kBQ);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sV + kVStages * kKVBytes);
   uint64_t* q_full = bar;          // [2] Q landed
   uint64_t* q_empty = bar + 2;     // [2] last S MMA of the item that read Q completed
   uint64_t* k_full = bar + 4;                 // [kKStages]
   uint64_t* k_empty = k_full + kKStages;      // [kKStages] S MMA that read the K tile completed
   uint64_t* v_full = k_empty + kKStages;      // [kVStages]
   uint64_t* v_empty = v_full + kVStages;      // [kVStages] P V MMA that read the V tile completed
-  uint64_t* s_full = v_empty + kVStages;      // [2] scores in TMEM
-  uint64_t* p_full = s_full + 2;              // [2] P written over S in TMEM by the 8 softmax warps
-  uint64_t* p_empty = p_full + 2;             // [2] P V MMA of the tile completed (O updated)
-  uint64_t* o_empty = p_empty + 2;            // [2] an item's O read out by the 8 softmax warps
-  uint64_t* drain = o_empty + 2;
+  uint64_t* s_full = v_empty + kVStages;      // [kSBufs] scores in TMEM
+  uint64_t* p_full = s_full + kSBufs;         // [kSBufs] P written over S in TMEM by the 8 softmax warps
+  uint64_t* p_empty = p_full + kSBufs;        // [kSBufs] P V MMA of the tile completed (O updated)
+  uint64_t* o_empty = p_empty + kSBufs;       // [1] the previous item's O read out by the 8 softmax warps
+  uint64_t* drain = o_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -240,11 +232,13 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
     for (int b = 0; b < 2; ++b) {
       mbar_init(&q_full[b], 1);
       mbar_init(&q_empty[b], 1);
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 8);
-      mbar_init(&p_empty[b], 1);
-      mbar_init(&o_empty[b], 8);
     }
+    for (int b = 0; b < kSBufs; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], kSoftmaxWarps);
+      mbar_init(&p_empty[b], 1);
+    }
+    mbar_init(o_empty, kSoftmaxWarps);
     for (int b = 0; b < kKStages; ++b) {
       mbar_init(&k_full[b], 1);
       mbar_init(&k_empty[b], 1);
@@ -266,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  static_assert((13 + 2 * (kKStages + kVStages)) * 8 + 8 <= 512, "barrier area");
+  static_assert((4 + 3 * kSBufs + 1 + 2 * (kKStages + kVStages) + 1) * 8 + 8 <= 512, "barrier area");
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producers
@@ -320,21 +314,19 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      Walk ws, wp;  // S runs two tiles ahead of P V
+      Walk ws, wp;  // S runs kSBufs tiles ahead of P V
       ws.init(tiles, n_tiles, n_items, window_half);
       wp.init(tiles, n_tiles, n_items, window_half);
-      int ks = 0, vs = 0;
-      uint32_t kph = 0, vph = 0, gs = 0, gp = 0;
-      // Shared-memory descriptors of every ring slot, built once.  Advancing 16 keys (K-major,
-      // 32 bytes) or 16 rows (MN-major V, 2048 bytes) adds to the 16-byte address field.
-      // Slots are picked with selects (the address field is the only difference), keeping the
-      // descriptors in registers.
-      static_assert(kKStages == 3 && kVStages == 2, "slot selects below");
+      int ks = 0, vs = 0, sb = 0, pb = 0;  // ring slots and score buffers of the next S / P V
+      uint32_t kph = 0, vph = 0, pph = 0;
+      // Shared-memory descriptors of the ring bases, built once.  Advancing 16 keys (K-major,
+      // 32 bytes), 16 rows (MN-major V, 2048 bytes) or one ring slot adds to the 16-byte address
+      // field.
       const uint64_t dq0 = smem_desc_sw128(smem_u32(sQ)), dq1 = dq0 + (kQBytes >> 4);
       const uint64_t dk0 = smem_desc_sw128(smem_u32(sK));
-      const uint64_t dv0 = smem_desc_sw128_mn(smem_u32(sV)), dv1 = dv0 + (kKVBytes >> 4);
-      // S[gs & 1] = Q K^T over the 64-wide head dim (4 MMAs of K = 16).  S[gs & 1] is free: the
-      // softmax warps released S of tile gs - 2 (p_full) before P V of that tile was issued.
+      const uint64_t dv0 = smem_desc_sw128_mn(smem_u32(sV));
+      // S[sb] = Q K^T over the 64-wide head dim (4 MMAs of K = 16).  S[sb] is free: P V of the
+      // tile that last used it was issued before this MMA, in this thread's order.
       auto issue_s = [&]() -> bool {
         const int qs = ws.i & 1;
         if (ws.j == 0 && !mbar_wait(&q_full[qs], (ws.i >> 1) & 1, abort_flag)) return false;
@@ -344,41 +336,38 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         const uint64_t bk = dk0 + static_cast<uint64_t>(ks * (kKVBytes >> 4));
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          tc_mma_f16(tmem_base + (gs & 1) * kBKV, aq + 2 * kk, bk + 2 * kk, kIdS, kk > 0 ? 1u : 0u);
-        tc_commit(&s_full[gs & 1]);
+          tc_mma_f16(tmem_base + sb * kBKV, aq + 2 * kk, bk + 2 * kk, kIdS, kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[sb]);
         tc_commit(&k_empty[ks]);
         if (ws.last_tile()) tc_commit(&q_empty[qs]);
         if (++ks == kKStages) { ks = 0; kph ^= 1u; }
-        ++gs;
+        if (++sb == kSBufs) sb = 0;
         ws.next(tiles, n_tiles, n_items, window_half);
         return true;
       };
       bool ok = true;
-      if (ws.valid(n_items)) ok = issue_s();
-      if (ok && ws.valid(n_items)) ok = issue_s();
+      for (int f = 0; f < kSBufs && ok && ws.valid(n_items); ++f) ok = issue_s();
       while (ok && wp.valid(n_items)) {
-        const int b = gp & 1;
-        const uint32_t ph = (gp >> 1) & 1;
-        const int os = wp.i & 1;  // O buffer of the item
-        // O[os] (+)= P V: P (16-bit, written over S[b] in TMEM: 128 lanes x 32 columns) is the A
+        // O (+)= P V: P (16-bit, written over S[pb] in TMEM: 128 lanes x 32 columns) is the A
         // operand, V is MN-major in shared memory (keys x head dim).  An item's first tile
-        // overwrites O[os], once the item two back has been read out of it.  S of tile gp + 2
-        // reuses S[b] only after this MMA, in this thread's issue order.
-        if ((wp.j == 0 && !mbar_wait(&o_empty[os], ((wp.i >> 1) & 1) ^ 1u, abort_flag)) ||
-            !mbar_wait_spin(&p_full[b], ph, abort_flag) || !mbar_wait(&v_full[vs], vph, abort_flag)) {
+        // overwrites O once the previous item has been read out of it (o_empty; a fresh
+        // barrier passes the first item).  S of tile gp + kSBufs reuses S[pb] only after this
+        // MMA, in this thread's issue order.
+        if ((wp.j == 0 && !mbar_wait(o_empty, (wp.i & 1) ^ 1u, abort_flag)) ||
+            !mbar_wait_spin(&p_full[pb], pph, abort_flag) || !mbar_wait(&v_full[vs], vph, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t bv = vs ? dv1 : dv0;
+        const uint64_t bv = dv0 + static_cast<uint64_t>(vs * (kKVBytes >> 4));
 #pragma unroll
         for (int kk = 0; kk < kBKV / 16; ++kk)
-          tc_mma_f16_ts(tmem_base + 2 * kBKV + os * kD, tmem_base + b * kBKV + 8 * kk, bv + 128 * kk,
-                        kIdO, (wp.j > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tmem_base + kOCol, tmem_base + pb * kBKV + 8 * kk, bv + 128 * kk, kIdO,
+                        (wp.j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&v_empty[vs]);
-        tc_commit(&p_empty[b]);
+        tc_commit(&p_empty[pb]);
         if (++vs == kVStages) { vs = 0; vph ^= 1u; }
-        ++gp;
+        if (++pb == kSBufs) { pb = 0; pph ^= 1u; }
         wp.next(tiles, n_tiles, n_items, window_half);
         if (ws.valid(n_items)) ok = issue_s();
       }
@@ -392,144 +381,145 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
     }
   } else {
     // ---------------------------------------------------------------- softmax
-    // Warp w (2..9) owns TMEM lanes of quadrant w % 4 and the 32 keys (and 32 O columns) of half
-    // (w - 2) / 4 of each tile; warps w and w + 4 share their rows through xmax / xsum.
-    const int half = (warp - 2) >> 2;
+    // Warp w (2..5) owns the 32 query rows of TMEM lane quadrant w % 4 and all 64 keys of each
+    // tile: one row per thread, so the row max, the sum and the rescaling stay in the thread.
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // query row of the item (= TMEM lane)
-    const int pair_id = 1 + quad;    // named barrier of the two warps of these rows
     const uint32_t trow = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     Walk wk;
     wk.init(tiles, n_tiles, n_items, window_half);
-    // Reference max m (log2 units, kNone until a key is visible) and this half's sum l of the row
-    // for the current item.  P = exp2(s - m) accumulates into the item's O in TMEM; m only moves
-    // when a tile's max exceeds it by more than kRescale (then O and l are rescaled), so P stays
-    // <= 2^kRescale.  Both halves of a row apply the same updates to m.
+    // Reference max m (log2 units, kNone until a key is visible) and sum l of the row for the
+    // current item.  P = exp2(s - m) accumulates into O in TMEM; m only moves when a tile's max
+    // exceeds it by more than kRescale (then O and l are rescaled), so P stays <= 2^kRescale.
     constexpr float kRescale = 8.f;
     constexpr float kNone = -1e30f;
     float m = kNone, l = 0.f;
-    // The finished item whose context row is written after the next item's first tile, so its
-    // last P V MMA completes behind that tile's softmax.
+    // The finished item whose context row is written after the next item's first P, so its last
+    // P V MMA completes behind that tile's softmax.
     bool fin = false, fin_live = false;
-    int fin_slot = 0, fin_b = 0;
+    int fin_b = 0;
+    float fin_l = 0.f;
     uint32_t fin_ph = 0, fin_off = 0;  // fin_off: element offset (T * H < 2^31, host-checked)
-    uint32_t g = 0;
+    // Score buffer and barrier parity of tile g.
+    int b = 0;
+    uint32_t ph = 0;
     bool fail = false;  // a wait of this thread expired or another role aborted
+    const uint64_t sl2 = f2_pack(scale_log2, scale_log2);
 
     for (;;) {
       const bool have = wk.valid(n_items);
-      const int b = g & 1;
-      const uint32_t ph = (g >> 1) & 1;
       const int qi = wk.q0 + r;
-      int cls = 0;
-      float sv[32];
       if (have) {
         if (wk.j == 0) {
           m = kNone;
           l = 0.f;
         }
         const int qa = wk.q0 + quad * 32;
-        const int kb = (wk.t_lo + wk.j) * kBKV + 32 * half;
-        cls = half_class(kb, wk.L, qa, qa + 31, window_half);
-        // Every warp waits for every tile's scores.  S of tile g is committed after the MMA thread
-        // issued P V of tile g - 2 and tcgen05.commit tracks every earlier MMA of that thread, so
-        // this wait also means: P slot b is free, and P V of g - 2 (so of g - 3 as well) has
-        // updated O.  The rescale and read-out waits on p_empty below therefore always target
-        // the barrier's current phase.
+        const int kb = (wk.t_lo + wk.j) * kBKV;
+        const int cls0 = half_class(kb, wk.L, qa, qa + 31, window_half);
+        const int cls1 = half_class(kb + 32, wk.L, qa, qa + 31, window_half);
+        // S of tile g is committed after the MMA thread issued P V of tile g - kSBufs, and
+        // tcgen05.commit tracks every earlier MMA of that thread: this wait also means that P V
+        // of g - kSBufs (and every earlier tile) has updated O, so the rescale and read-out
+        // waits on p_empty below (tiles g - 1 and later) target the barrier's current phase.
         fail = fail || !__all_sync(0xffffffffu, mbar_wait(&s_full[b], ph, abort_flag));
+        if (fail) break;
+        float s0[32], s1[32];
+        tc_fence_after();
+        tmem_ld32(trow + b * kBKV, s0);
+        tmem_ld32(trow + b * kBKV + 32, s1);
+        tc_wait_ld();
         float mt = -INFINITY;
-        if (!fail && cls) {
-          tc_fence_after();
-          tmem_ld32(trow + b * kBKV + 32 * half, sv);
-          tc_wait_ld();
-          mt = masked_max(sv, cls, kb, wk.L, qi, window_half) * scale_log2;
-        }
-        xmax[((g & 1) * 2 + half) * kBQ + r] = mt;
-      }
-      // Exchange the half-row maxima (and any failure) with the partner warp.
-      if (pair_any(pair_id, fail)) break;
-      if (have) {
-        const float mt = fmaxf(xmax[((g & 1) * 2 + half) * kBQ + r], xmax[((g & 1) * 2 + (half ^ 1)) * kBQ + r]);
+        if (cls0) mt = masked_max(s0, cls0, kb, wk.L, qi, window_half);
+        if (cls1) mt = fmaxf(mt, masked_max(s1, cls1, kb + 32, wk.L, qi, window_half));
+        mt *= scale_log2;
         // A row that has seen no key yet (its O row is 0) adopts the tile's max; a row whose max
         // grew by more than kRescale rescales its O and l (rare: the warp waits for the previous
-        // P V into O, then reads, scales and rewrites its 32 lanes x 32 columns).
+        // P V into O, then reads, scales and rewrites its 32 lanes x 64 columns).
         const bool need = m != kNone && mt > m + kRescale;
         if (m == kNone) m = fmaxf(m, mt);
         if (__any_sync(0xffffffffu, need)) {
-          fail = !__all_sync(0xffffffffu, mbar_wait(&p_empty[b ^ 1], ((g - 1) >> 1) & 1, abort_flag));
-          if (!fail) {
-            tc_fence_after();
-            const float alpha = need ? ex2(m - mt) : 1.f;
-            const uint32_t ocol = trow + 2 * kBKV + (wk.i & 1) * kD + 32 * half;
-            float t[32];
-            tmem_ld32(ocol, t);
+          // P V of tile g - 1: the buffer before b, one phase back when b wrapped around.
+          const int pb = b == 0 ? kSBufs - 1 : b - 1;
+          const uint32_t pph = b == 0 ? ph ^ 1u : ph;
+          fail = !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb], pph, abort_flag));
+          if (fail) break;
+          tc_fence_after();
+          const float alpha = need ? ex2(m - mt) : 1.f;
+          float t[32];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            tmem_ld32(trow + kOCol + 32 * h, t);
             tc_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] *= alpha;
-            tmem_st32(ocol, t);
-            tc_wait_st();
-            if (need) {
-              l *= alpha;
-              m = mt;
-            }
+            tmem_st32(trow + kOCol + 32 * h, t);
+          }
+          tc_wait_st();
+          if (need) {
+            l *= alpha;
+            m = mt;
           }
         }
-        if (!fail) {
-          // P of this half's 32 keys, as 16 packed pairs, over the first half of S[b]: both
-          // warps of the row loaded their scores before the exchange barrier above, so this
-          // store cannot overwrite scores still to be read.
-          const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m, -m);
-          uint64_t ps[2] = {0ull, 0ull};  // two packed partial sums (f32 zero bits)
-          uint32_t w[16];
-          make_p<T>(cls != 0, sv, sl2, nm2, ps, w);
-          tmem_st16(trow + b * kBKV + 16 * half, w);
-          float p0, p1, p2, p3;
-          f2_unpack(ps[0], p0, p1);
-          f2_unpack(ps[1], p2, p3);
-          l += (p0 + p1) + (p2 + p3);
-          tc_wait_st();  // P is in TMEM before the MMA thread may read it
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&p_full[b]);
-        }
+        // P of the 64 keys as 32 packed 16-bit pairs over the first 32 columns of S[b] (the
+        // scores were all read above).
+        const uint64_t nm2 = f2_pack(-m, -m);
+        uint64_t ps[2] = {0ull, 0ull};  // two packed partial sums (f32 zero bits)
+        uint32_t w[16];
+        make_p<T>(cls0 != 0, s0, sl2, nm2, ps, w);
+        tmem_st16(trow + b * kBKV, w);
+        make_p<T>(cls1 != 0, s1, sl2, nm2, ps, w);
+        tmem_st16(trow + b * kBKV + 16, w);
+        float p0, p1, p2, p3;
+        f2_unpack(ps[0], p0, p1);
+        f2_unpack(ps[1], p2, p3);
+        l += (p0 + p1) + (p2 + p3);
+        tc_wait_st();  // P is in TMEM before the MMA thread may read it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[b]);
       }
       if (fin) {
-        // Context row = O / (l_half0 + l_half1), read from TMEM once the item's last P V
-        // completed (p_empty of its slot); then O[fin_slot] is released for the item two ahead.
-        fail = fail || !__all_sync(0xffffffffu, mbar_wait(&p_empty[fin_b], fin_ph, abort_flag));
-        if (pair_any(pair_id, fail)) break;
-        const float lt = xsum[(fin_slot * 2) * kBQ + r] + xsum[(fin_slot * 2 + 1) * kBQ + r];
-        const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+        // Context row = O / l, read from TMEM once the item's last P V completed (p_empty of its
+        // score buffer); then O is released for the next item's first P V (o_empty).
+        fail = !__all_sync(0xffffffffu, mbar_wait(&p_empty[fin_b], fin_ph, abort_flag));
+        if (fail) break;
+        const float inv = fin_l > 0.f ? 1.0f / fin_l : 0.f;
         tc_fence_after();
         float t[32];
-        tmem_ld32(trow + 2 * kBKV + fin_slot * kD + 32 * half, t);
-        tc_wait_ld();
-        if (fin_live) {
-          uint4* dst = reinterpret_cast<uint4*>(ctx + fin_off + 32 * half);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float f[8];
+        for (int h = 0; h < 2; ++h) {
+          tmem_ld32(trow + kOCol + 32 * h, t);
+          tc_wait_ld();
+          if (fin_live) {
+            uint4* dst = reinterpret_cast<uint4*>(ctx + fin_off + 32 * h);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = t[8 * c + e] * inv;
-            dst[c] = pack8<T>(f);
+            for (int c = 0; c < 4; ++c) {
+              float f[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = t[8 * c + e] * inv;
+              dst[c] = pack8<T>(f);
+            }
           }
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&o_empty[fin_slot]);
+        if (lane == 0) mbar_arrive(o_empty);
         fin = false;
       }
       if (!have) break;
       if (wk.last_tile()) {
         fin = true;
         fin_live = qi < wk.L;
-        fin_slot = wk.i & 1;
         fin_b = b;
         fin_ph = ph;
+        fin_l = l;
         fin_off = static_cast<uint32_t>((wk.s0 + qi) * H + wk.head(n_tiles) * kD);
-        xsum[(fin_slot * 2 + half) * kBQ + r] = l;
       }
-      ++g;
+      if (++b == kSBufs) {
+        b = 0;
+        ph ^= 1u;
+      }
       wk.next(tiles, n_tiles, n_items, window_half);
     }
     if (fail && lane == 0) {
@@ -590,10 +580,21 @@ cudaError_t attention_varlen_tc(Act act, const void* qkv, void* ctx, int total_t
 }
 
 int fill_attention_tiles(const int* cu_seqlens, int n_seqs, int2* out) {
-  int t = 0;
+  // Longest sequences first: the persistent CTAs take items in this order (per head), so the
+  // items with the most key tiles start first and the short ones fill the end of each wave.
+  std::vector<int> order;
+  order.reserve(size_t(n_seqs > 0 ? n_seqs : 0));
   for (int b = 0; b < n_seqs; ++b) {
-    const int s0 = cu_seqlens[b], L = cu_seqlens[b + 1] - s0;
+    const int L = cu_seqlens[b + 1] - cu_seqlens[b];
     if (L < 0 || L > kMaxAttnSeq) return -1;
+    if (L > 0) order.push_back(b);
+  }
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+    return cu_seqlens[a + 1] - cu_seqlens[a] > cu_seqlens[b + 1] - cu_seqlens[b];
+  });
+  int t = 0;
+  for (int b : order) {
+    const int s0 = cu_seqlens[b], L = cu_seqlens[b + 1] - s0;
     for (int q0 = 0; q0 < L; q0 += kBQ) out[t++] = make_int2(s0, L | (q0 << 16));
   }
   return t;
