@@ -5,9 +5,11 @@
 // persistent: two CTAs per SM each walk the items blockIdx.x, blockIdx.x + gridDim.x, ...
 // (head-major, so the items in flight share their sequences' K/V in L2), and every ring below
 // runs across item boundaries, so the next item's Q and K/V load while the current one finishes.
-// Warp roles (320 threads):
-//   warp 0      TMA producers: lane 0 loads Q per item (2 buffers) and K tiles (4-deep ring),
-//               lane 1 loads V tiles (3-deep ring), 64 keys per tile,
+// Warp roles (192 threads):
+//   warp 0      TMA producers: lane 0 loads Q per item (2 buffers) and K tiles, lane 1 loads V
+//               tiles, 64 keys per tile; both rings are as deep as the score ring, so slot
+//               g % 3 of K is free once S of tile g completed (s_full) and slot g % 3 of V once
+//               P V of tile g completed (p_empty): the MMA thread commits once per MMA group,
 //   warp 1      TMEM owner and single-thread tcgen05.mma issuer,
 //   warps 2..5  softmax: warp w owns TMEM lane quadrant w % 4 (32 query rows, one per thread)
 //               and all 64 keys of every tile.
@@ -47,8 +49,8 @@ constexpr int kD = 64;         // head dim
 // same columns) has been issued.  K is on the critical path (S needs it kSBufs tiles ahead of
 // the softmax) and is loaded kKStages tiles ahead; V is needed only when P V is issued.
 constexpr int kSBufs = 3;
-constexpr int kKStages = 4;
-constexpr int kVStages = 3;
+constexpr int kKStages = 3;  // == kSBufs: slot g % 3 of K is free when S of tile g completes
+constexpr int kVStages = 3;  // == kSBufs: slot g % 3 of V is free when P V of tile g completes
 constexpr int kQBytes = kBQ * kD * 2;    // 16 KB
 constexpr int kKVBytes = kBKV * kD * 2;  // 8 KB
 constexpr int kOCol = kSBufs * kBKV;     // O after the score buffers
@@ -215,12 +217,10 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
   uint64_t* q_full = bar;          // [2] Q landed
   uint64_t* q_empty = bar + 2;     // [2] last S MMA of the item that read Q completed
   uint64_t* k_full = bar + 4;                 // [kKStages]
-  uint64_t* k_empty = k_full + kKStages;      // [kKStages] S MMA that read the K tile completed
-  uint64_t* v_full = k_empty + kKStages;      // [kVStages]
-  uint64_t* v_empty = v_full + kVStages;      // [kVStages] P V MMA that read the V tile completed
-  uint64_t* s_full = v_empty + kVStages;      // [kSBufs] scores in TMEM
+  uint64_t* v_full = k_full + kKStages;       // [kVStages]
+  uint64_t* s_full = v_full + kVStages;       // [kSBufs] scores in TMEM (K slot free again)
   uint64_t* p_full = s_full + kSBufs;         // [kSBufs] P written over S in TMEM by the 8 softmax warps
-  uint64_t* p_empty = p_full + kSBufs;        // [kSBufs] P V MMA of the tile completed (O updated)
+  uint64_t* p_empty = p_full + kSBufs;        // [kSBufs] P V MMA of the tile completed (O updated, V slot free)
   uint64_t* o_empty = p_empty + kSBufs;       // [1] the previous item's O read out by the 8 softmax warps
   uint64_t* drain = o_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -239,14 +239,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
       mbar_init(&p_empty[b], 1);
     }
     mbar_init(o_empty, kSoftmaxWarps);
-    for (int b = 0; b < kKStages; ++b) {
-      mbar_init(&k_full[b], 1);
-      mbar_init(&k_empty[b], 1);
-    }
-    for (int b = 0; b < kVStages; ++b) {
-      mbar_init(&v_full[b], 1);
-      mbar_init(&v_empty[b], 1);
-    }
+    for (int b = 0; b < kKStages; ++b) mbar_init(&k_full[b], 1);
+    for (int b = 0; b < kVStages; ++b) mbar_init(&v_full[b], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -260,7 +254,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  static_assert((4 + 3 * kSBufs + 1 + 2 * (kKStages + kVStages) + 1) * 8 + 8 <= 512, "barrier area");
+  static_assert((4 + 3 * kSBufs + 1 + kKStages + kVStages + 1) * 8 + 8 <= 512, "barrier area");
+  static_assert(kKStages == kSBufs && kVStages == kSBufs, "K / V slots are released by s_full / p_empty");
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producers
@@ -276,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
       uint32_t q_iss = 0, q_par = 0, iss = 0, par = 0;
       const int stages = kq ? kKStages : kVStages;
       uint64_t* full = kq ? k_full : v_full;
-      uint64_t* empty = kq ? k_empty : v_empty;
+      uint64_t* empty = kq ? s_full : p_empty;
       uint8_t* ring = kq ? sK : sV;
       const int col0 = (kq ? H : 2 * H);
       int rs = 0;
@@ -338,7 +333,6 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         for (int kk = 0; kk < kD / 16; ++kk)
           tc_mma_f16(tmem_base + sb * kBKV, aq + 2 * kk, bk + 2 * kk, kIdS, kk > 0 ? 1u : 0u);
         tc_commit(&s_full[sb]);
-        tc_commit(&k_empty[ks]);
         if (ws.last_tile()) tc_commit(&q_empty[qs]);
         if (++ks == kKStages) { ks = 0; kph ^= 1u; }
         if (++sb == kSBufs) sb = 0;
@@ -364,7 +358,6 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         for (int kk = 0; kk < kBKV / 16; ++kk)
           tc_mma_f16_ts(tmem_base + kOCol, tmem_base + pb * kBKV + 8 * kk, bv + 128 * kk, kIdO,
                         (wp.j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&v_empty[vs]);
         tc_commit(&p_empty[pb]);
         if (++vs == kVStages) { vs = 0; vph ^= 1u; }
         if (++pb == kSBufs) { pb = 0; pph ^= 1u; }
