@@ -293,6 +293,15 @@ int rv_op_gemm(int32_t act_dtype, const void* a, const void* b, void* c, int32_t
 int rv_op_attention(int32_t act_dtype, const void* qkv, void* ctx_out, const int32_t* cu_seqlens_host,
                     int32_t n_seqs, int32_t num_heads, int32_t head_dim, int32_t window_half,
                     float scale, void* stream);
+/* Test hook of the device-side error path (no counterpart in the reference; the reference's
+ * contract is that errors propagate, backend/mod.rs:53-54).  While enabled, every tcgen05
+ * attention launch (rv_op_attention and the attention of rv_embed_*) withholds the score signal
+ * of each persistent CTA's first tile and bounds every pipeline wait by wait_limit_cycles SM
+ * cycles: the softmax warps' wait expires, every role leaves through the kernel's bounded-wait
+ * exit (copies and MMAs in flight are drained, TMEM is freed), and the call returns RV_E_DEVICE.
+ * Nothing faults, traps or spins without bound.  enable = 0 restores normal launches.  Process
+ * wide; for tests only. */
+int rv_debug_stall_attention(int32_t enable, int64_t wait_limit_cycles);
 /* out = LN(in) * gamma (+ beta); 16-bit rows. */
 int rv_op_layernorm(int32_t act_dtype, const void* in, void* out, int32_t rows, int32_t hidden,
                     const float* gamma, const float* beta, float eps, void* stream);

@@ -112,6 +112,7 @@ SIGNATURES = {
     "rv_index_find_duplicates": (C.c_int, [vp, f32, i64, vp, vp, vp, vp, vp]),
     "rv_op_gemm": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "rv_op_attention": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, f32, vp]),
+    "rv_debug_stall_attention": (C.c_int, [i32, i64]),
     "rv_op_layernorm": (C.c_int, [i32, vp, vp, i32, i32, vp, vp, f32, vp]),
 }
 

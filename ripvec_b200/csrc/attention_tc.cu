@@ -32,6 +32,7 @@
 // 1/sqrt(d), additive -1e9 masks for padding and |i-j| > window/2, max-subtracted softmax, P V);
 // masked keys get weight 0 exactly, as exp(-1e9 - max) does in f32.
 #include <algorithm>
+#include <atomic>
 #include <vector>
 
 #include "common.cuh"
@@ -202,7 +203,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
                                                               const int2* __restrict__ tiles,
                                                               int n_tiles, int n_items, int H,
                                                               int window_half, float scale_log2,
-                                                              unsigned int* err) {
+                                                              unsigned int* err, long long wait_limit,
+                                                              int stall) {
   constexpr bool kBf = Elem<T>::kBf16;
   constexpr uint32_t kIdS = idesc_f16(kBQ, kBKV, kBf);
   constexpr uint32_t kIdO = idesc_f16_bmn(kBQ, kD, kBf);
@@ -280,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         if (kq && wk.j == 0) {
           const int qs = wk.i & 1;
           const uint32_t qph = (wk.i >> 1) & 1;
-          if (!mbar_wait(&q_empty[qs], qph ^ 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&q_empty[qs], qph ^ 1u, abort_flag, wait_limit)) { ok = false; break; }
           mbar_arrive_expect_tx(&q_full[qs], kQBytes);
           tma_load_2d(sQ + qs * kQBytes, &tmQKV, &q_full[qs], wk.head(n_tiles) * kD, wk.s0 + wk.q0);
           tma_load_2d(sQ + qs * kQBytes + kQBytes / 2, &tmQKV, &q_full[qs], wk.head(n_tiles) * kD,
@@ -289,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
           q_par = (q_par & ~(1u << qs)) | (qph << qs);
         }
         const int row = wk.s0 + (wk.t_lo + wk.j) * kBKV;
-        if (!mbar_wait(&empty[rs], rph ^ 1u, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&empty[rs], rph ^ 1u, abort_flag, wait_limit)) { ok = false; break; }
         mbar_arrive_expect_tx(&full[rs], kKVBytes);
         tma_load_2d(ring + rs * kKVBytes, &tmQKV, &full[rs], col0 + wk.head(n_tiles) * kD, row);
         iss |= 1u << rs;
@@ -300,11 +302,13 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
       if (!ok) {
         *abort_flag = 1;
         atomicOr(err, kErrWaitTimeout);
-        for (int b = 0; b < 2; ++b)
-          if (q_iss & (1u << b)) wait_done(&q_full[b], (q_par >> b) & 1u);
-        for (int b = 0; b < stages; ++b)
-          if (iss & (1u << b)) wait_done(&full[b], (par >> b) & 1u);
       }
+      // Every issued copy has landed before the CTA can exit, also when another role aborted
+      // before consuming it (on the normal path these waits pass at once).
+      for (int b = 0; b < 2; ++b)
+        if (q_iss & (1u << b)) wait_done(&q_full[b], (q_par >> b) & 1u);
+      for (int b = 0; b < stages; ++b)
+        if (iss & (1u << b)) wait_done(&full[b], (par >> b) & 1u);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
@@ -324,15 +328,17 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
       // tile that last used it was issued before this MMA, in this thread's order.
       auto issue_s = [&]() -> bool {
         const int qs = ws.i & 1;
-        if (ws.j == 0 && !mbar_wait(&q_full[qs], (ws.i >> 1) & 1, abort_flag)) return false;
-        if (!mbar_wait(&k_full[ks], kph, abort_flag)) return false;
+        if (ws.j == 0 && !mbar_wait(&q_full[qs], (ws.i >> 1) & 1, abort_flag, wait_limit)) return false;
+        if (!mbar_wait(&k_full[ks], kph, abort_flag, wait_limit)) return false;
         tc_fence_after();
         const uint64_t aq = qs ? dq1 : dq0;
         const uint64_t bk = dk0 + static_cast<uint64_t>(ks * (kKVBytes >> 4));
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
           tc_mma_f16(tmem_base + sb * kBKV, aq + 2 * kk, bk + 2 * kk, kIdS, kk > 0 ? 1u : 0u);
-        tc_commit(&s_full[sb]);
+        // Test hook (rv_debug_stall_attention): the first tile's scores are never signalled, so
+        // the softmax warps' bounded wait expires and the launch ends with kErrWaitTimeout.
+        if (!(stall && ws.w == static_cast<int>(blockIdx.x) && ws.j == 0)) tc_commit(&s_full[sb]);
         if (ws.last_tile()) tc_commit(&q_empty[qs]);
         if (++ks == kKStages) { ks = 0; kph ^= 1u; }
         if (++sb == kSBufs) sb = 0;
@@ -347,8 +353,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         // overwrites O once the previous item has been read out of it (o_empty; a fresh
         // barrier passes the first item).  S of tile gp + kSBufs reuses S[pb] only after this
         // MMA, in this thread's issue order.
-        if ((wp.j == 0 && !mbar_wait(o_empty, (wp.i & 1) ^ 1u, abort_flag)) ||
-            !mbar_wait_spin(&p_full[pb], pph, abort_flag) || !mbar_wait(&v_full[vs], vph, abort_flag)) {
+        if ((wp.j == 0 && !mbar_wait(o_empty, (wp.i & 1) ^ 1u, abort_flag, wait_limit)) ||
+            !mbar_wait_spin(&p_full[pb], pph, abort_flag, wait_limit) || !mbar_wait(&v_full[vs], vph, abort_flag, wait_limit)) {
           ok = false;
           break;
         }
@@ -415,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         // tcgen05.commit tracks every earlier MMA of that thread: this wait also means that P V
         // of g - kSBufs (and every earlier tile) has updated O, so the rescale and read-out
         // waits on p_empty below (tiles g - 1 and later) target the barrier's current phase.
-        fail = fail || !__all_sync(0xffffffffu, mbar_wait(&s_full[b], ph, abort_flag));
+        fail = fail || !__all_sync(0xffffffffu, mbar_wait(&s_full[b], ph, abort_flag, wait_limit));
         if (fail) break;
         float s0[32], s1[32];
         tc_fence_after();
@@ -435,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
           // P V of tile g - 1: the buffer before b, one phase back when b wrapped around.
           const int pb = b == 0 ? kSBufs - 1 : b - 1;
           const uint32_t pph = b == 0 ? ph ^ 1u : ph;
-          fail = !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb], pph, abort_flag));
+          fail = !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb], pph, abort_flag, wait_limit));
           if (fail) break;
           tc_fence_after();
           const float alpha = need ? ex2(m - mt) : 1.f;
@@ -475,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
       if (fin) {
         // Context row = O / l, read from TMEM once the item's last P V completed (p_empty of its
         // score buffer); then O is released for the next item's first P V (o_empty).
-        fail = !__all_sync(0xffffffffu, mbar_wait(&p_empty[fin_b], fin_ph, abort_flag));
+        fail = !__all_sync(0xffffffffu, mbar_wait(&p_empty[fin_b], fin_ph, abort_flag, wait_limit));
         if (fail) break;
         const float inv = fin_l > 0.f ? 1.0f / fin_l : 0.f;
         tc_fence_after();
@@ -528,6 +534,11 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
   }
 }
 
+// Test hook state (attention_set_stall): withhold the first score signal of every CTA and use a
+// short wait limit, so that a launch ends through the bounded-wait error path.
+std::atomic<int> g_stall{0};
+std::atomic<long long> g_stall_limit{kWaitLimitCycles};
+
 template <typename T>
 cudaError_t launch_attn_tc(const CUtensorMap& tm, void* ctx, const int2* tiles, int n_tiles,
                            int num_heads, int window_half, float scale, unsigned int* err,
@@ -546,8 +557,10 @@ cudaError_t launch_attn_tc(const CUtensorMap& tm, void* ctx, const int2* tiles, 
   const int slots = 2 * device_sm_count();
   const int grid = n_items < slots ? n_items : slots;
   const float scale_log2 = scale * 1.4426950408889634f;
+  const int stall = g_stall.load(std::memory_order_relaxed);
+  const long long limit = stall ? g_stall_limit.load(std::memory_order_relaxed) : kWaitLimitCycles;
   attn_tc_kernel<T><<<grid, kThreads, kSmem, st>>>(tm, static_cast<T*>(ctx), tiles, n_tiles, n_items,
-                                                   num_heads * kD, window_half, scale_log2, err);
+                                                   num_heads * kD, window_half, scale_log2, err, limit, stall);
   return cudaGetLastError();
 }
 
@@ -570,6 +583,11 @@ cudaError_t attention_varlen_tc(Act act, const void* qkv, void* ctx, int total_t
   if (act == Act::kBf16)
     return launch_attn_tc<__nv_bfloat16>(tm, ctx, tiles, n_tiles, num_heads, window_half, scale, err, st);
   return launch_attn_tc<__half>(tm, ctx, tiles, n_tiles, num_heads, window_half, scale, err, st);
+}
+
+void attention_set_stall(int enable, long long wait_limit_cycles) {
+  g_stall_limit.store(wait_limit_cycles > 0 ? wait_limit_cycles : kWaitLimitCycles, std::memory_order_relaxed);
+  g_stall.store(enable ? 1 : 0, std::memory_order_relaxed);
 }
 
 int fill_attention_tiles(const int* cu_seqlens, int n_seqs, int2* out) {

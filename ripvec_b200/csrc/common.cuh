@@ -66,7 +66,8 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 // Same bounds as mbar_wait, without the sleep hint: for a single thread on a latency-critical
 // path (the attention MMA issuer), which should see a completed phase as soon as possible.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
@@ -74,12 +75,14 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, v
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitLimitCycles) return false;
+    if (clock64() - t0 > limit) return false;
   }
 }
 // Waits for the phase with the given parity to complete.  Returns false (and never blocks for
-// more than kWaitLimitCycles) when the wait gives up or another role of the CTA raised *abort.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// more than `limit` SM cycles, kWaitLimitCycles by default) when the wait gives up or another
+// role of the CTA raised *abort.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
@@ -87,7 +90,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     for (int i = 0; i < 8; ++i)
       if (mbar_try_wait_sleep(bar, parity)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitLimitCycles) return false;
+    if (clock64() - t0 > limit) return false;
   }
 }
 

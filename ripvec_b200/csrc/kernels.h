@@ -98,6 +98,10 @@ constexpr int kMaxAttnSeq = 32767;
 // at most total_tokens / 128 + n_seqs) and returns their count, or -1 when a length is negative
 // or above kMaxAttnSeq.
 int fill_attention_tiles(const int* cu_seqlens, int n_seqs, int2* out);
+// Test hook of the device error path: while enabled, every tcgen05 attention launch withholds
+// the score signal of each CTA's first tile and bounds its waits by wait_limit_cycles, so the
+// launch ends through its bounded-wait exit and reports kErrWaitTimeout.
+void attention_set_stall(int enable, long long wait_limit_cycles);
 
 // f32 -> 16-bit conversion (weights upload), n elements.
 cudaError_t convert_f32(Act act, const float* in, void* out, int64_t n, cudaStream_t st);

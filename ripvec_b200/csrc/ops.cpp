@@ -124,6 +124,12 @@ int rv_op_attention(int32_t act_dtype, const void* qkv, void* ctx_out, const int
   return rc;
 }
 
+int rv_debug_stall_attention(int32_t enable, int64_t wait_limit_cycles) {
+  if (enable && wait_limit_cycles <= 0) return RV_E_INVALID;
+  rv::attention_set_stall(enable, wait_limit_cycles);
+  return RV_OK;
+}
+
 int rv_op_layernorm(int32_t act_dtype, const void* in, void* out, int32_t rows, int32_t hidden,
                     const float* gamma, const float* beta, float eps, void* stream) {
   if (act_dtype != RV_DTYPE_BF16 && act_dtype != RV_DTYPE_F16) return RV_E_INVALID;
