@@ -12,7 +12,19 @@
 
 namespace rv {
 
-__device__ __forceinline__ float gelu_tanh_fast(float x) { return gelu_tanh(x); }
+// tanh-GELU through the identity 0.5 (1 + tanh(y)) = 1 / (1 + e^(-2y)):
+// gelu(x) = x / (1 + 2^(-2 log2(e) y)), y = sqrt(2/pi) (x + 0.044715 x^3).  The hardware base-2
+// exponential and reciprocal (ex2.approx, rcp.approx) give it to about 1e-6 relative over the
+// whole range, far below the 16-bit rounding of the stored result, in a handful of instructions
+// (tanhf costs several times more, and 1 + tanh(y) would cancel for negative x).
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+  const float k = -2.0f * 1.4426950408889634f * 0.7978845608028654f;  // -2 log2(e) sqrt(2/pi)
+  const float t = k * (x + 0.044715f * x * x * x);
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return x * r;
+}
 
 // x <- x + acc, then LayerNorm partials of the stored (rounded) row per 256-column tile.
 template <typename T>
@@ -32,6 +44,9 @@ struct TEpiResidualStats {
   }
   __device__ __forceinline__ void compute(Tile& t, int row, int col, const float* r, float (&v0)[32],
                                           float (&v1)[32], bool live) const {
+    // The 64 stored (rounded) values of this group, their mean and M2 (two passes, four partial
+    // sums each), then one pairwise (Chan) merge into the tile's running (n, mean, M2).
+    float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       float* v = (i < 4) ? &v0[8 * i] : &v1[8 * (i - 4)];
@@ -40,20 +55,25 @@ struct TEpiResidualStats {
       for (int j = 0; j < 8; ++j) o[j] = v[j] + r[8 * i + j];
       unpack8<T>(pack8<T>(o), o);  // the values as they will be stored
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = o[j];
-      float m = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) m += o[j];
-      m *= 0.125f;
-      float q = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q += (o[j] - m) * (o[j] - m);
-      const float tot = t.n + 8.f;
-      const float d = m - t.mean;
-      t.mean += d * (8.f / tot);
-      t.m2 += q + d * d * (t.n * 8.f / tot);
-      t.n = tot;
+      for (int j = 0; j < 8; ++j) {
+        v[j] = o[j];
+        s4[j & 3] += o[j];
+      }
     }
+    const float m = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.0f / 64.0f);
+    float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const float d = (i < 32 ? v0[i] : v1[i - 32]) - m;
+      q4[i & 3] = fmaf(d, d, q4[i & 3]);
+    }
+    const float q = (q4[0] + q4[1]) + (q4[2] + q4[3]);
+    const float tot = t.n + 64.f;
+    const float w = 64.f / tot;
+    const float d = m - t.mean;
+    t.mean += d * w;
+    t.m2 += q + d * d * (t.n * w);
+    t.n = tot;
     if (live && (col & 255) == 192)
       stats[static_cast<size_t>(row) * stats_ld + (col >> 8)] = make_float2(t.mean, t.m2);
   }
