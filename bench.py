@@ -775,7 +775,15 @@ def run_turboquant(args):
         torch.cuda.synchronize()
         clocks = sampler.stop()
         ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
-        passes = -(-nq // 4)  # the scan shares each code word among up to 4 queries
+        # passes over the codes: the scan shares each code word among up to 8 queries (then 4, 2, 1
+        # for the rest), as scan_qb in turbo_quant.cu
+        passes, left = 0, nq
+        while left > 0:
+            qb = 8
+            while qb > left:
+                qb //= 2
+            left -= qb
+            passes += 1
         code_bytes = passes * n_rows * (dim // 2) * 5
         ach = code_bytes / (ms / 1e3) / 1e9
         line = {"metric": "rank_turboquant queries/sec (PolarQuant 4-bit, 10M x 768)", "value": nq / (ms / 1e3),

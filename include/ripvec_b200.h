@@ -97,6 +97,21 @@ int rv_embed_varlen(rv_ctx* ctx, const int32_t* ids, const int32_t* cu_seqlens, 
 int rv_embed_varlen_device(rv_ctx* ctx, const int32_t* ids_dev, const int32_t* cu_seqlens_host,
                            int32_t n_seqs, void* out_dev, int32_t out_dtype, void* stream);
 
+/* Asynchronous form of rv_embed_varlen, for a caller that keeps the GPU fed while it tokenises the
+ * next chunks (the reference's bounded pipeline of tokeniser threads feeding the embedding stage,
+ * crates/ripvec-core/src/embed.rs:273-463).  rv_embed_submit copies the ids into the context's
+ * pinned staging, queues the copies and the forward of every packed batch on the context's
+ * stream and returns at once with a ticket; out_host must stay valid until rv_embed_wait on that
+ * ticket returns.  At most two batches are in flight: a submission whose batches need a busy
+ * staging slot first completes the oldest batch (moving its embeddings to its caller's buffer).
+ * Input errors (bad cu_seqlens, token ids outside the vocabulary) are returned by the submit;
+ * device errors of a job are returned by its wait.  rv_embed_wait returns when the embeddings of
+ * the ticket (and of every earlier ticket) are in their buffers; waiting on a ticket twice
+ * returns RV_OK. */
+int rv_embed_submit(rv_ctx* ctx, const int32_t* ids, const int32_t* cu_seqlens, int32_t n_seqs, float* out_host,
+                    int64_t* ticket);
+int rv_embed_wait(rv_ctx* ctx, int64_t ticket);
+
 /* embed_distributed over several backends (crates/ripvec-core/src/embed.rs:666-785): one host
  * thread per context (each context on its own GPU, or several on one), all taking runs of
  * consecutive chunks from one cursor in input order, each run sized to its context's token

@@ -72,6 +72,8 @@ SIGNATURES = {
     "rv_finalize": (C.c_int, [vp]),
     "rv_embed_varlen": (C.c_int, [vp, vp, vp, i32, vp]),
     "rv_embed_varlen_device": (C.c_int, [vp, vp, vp, i32, vp, i32, vp]),
+    "rv_embed_submit": (C.c_int, [vp, vp, vp, i32, vp, C.POINTER(i64)]),
+    "rv_embed_wait": (C.c_int, [vp, i64]),
     "rv_embed_varlen_multi": (C.c_int, [vp, i32, vp, vp, i32, vp]),
     "rv_max_tokens": (C.c_int, [vp]),
     "rv_hidden_dim": (C.c_int, [vp]),

@@ -143,6 +143,31 @@ class EmbedBackend:
         self._check(self._lib.rv_embed_varlen_device(self._h, L.ptr(ids_dev), cu.ctypes.data, len(cu) - 1,
                                                      L.ptr(out_dev), out_dtype, stream or None))
 
+    def submit(self, ids: np.ndarray, cu_seqlens: np.ndarray, out: np.ndarray | None = None):
+        """``rv_embed_submit``: queues the packed chunks and returns ``(ticket, out)`` at once; ``out``
+        ([n, hidden] f32) is filled when ``wait(ticket)`` returns and must be kept until then."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        cu = np.ascontiguousarray(cu_seqlens, np.int32)
+        n = len(cu) - 1
+        if out is None:
+            out = np.empty((max(n, 0), self.spec.hidden), np.float32)
+        t = C.c_int64(0)
+        self._check(self._lib.rv_embed_submit(self._h, ids.ctypes.data if ids.size else None, cu.ctypes.data, n,
+                                              out.ctypes.data, C.byref(t)))
+        self._pending = getattr(self, "_pending", {})
+        self._pending[t.value] = out  # the library writes into it until the wait
+        return t.value, out
+
+    def wait(self, ticket: int) -> None:
+        """``rv_embed_wait``: returns when the ticket's embeddings (and every earlier ticket's) are in
+        their output arrays."""
+        try:
+            self._check(self._lib.rv_embed_wait(self._h, ticket))
+        finally:
+            pend = getattr(self, "_pending", {})
+            for t in [t for t in pend if t <= ticket]:
+                pend.pop(t)
+
     def kernel_launches(self) -> int:
         return int(self._lib.rv_kernel_launches(self._h))
 

@@ -623,55 +623,133 @@ int validate_cu(rv_ctx* c, const int32_t* cu, int32_t n) {
 // Runs the packed batches covering sequences [0, n).  ids_src(b0, tokens) returns the device
 // pointer of the ids of the batch starting at sequence b0 (copying them first when needed);
 // out_dst(b0, nb, f32 src) moves the batch's embeddings to their destination.
+//
+// Batch rule (shared with the asynchronous path): consecutive sequences from b0 until the next
+// one would pass t_max tokens or n_max sequences.
+int32_t batch_end(const rv_ctx* c, const int32_t* cu, int32_t n, int32_t b0, int64_t* tokens) {
+  int32_t b1 = b0;
+  int64_t t = 0;
+  while (b1 < n && (b1 - b0) < c->n_max) {
+    const int64_t len = int64_t(cu[b1 + 1]) - cu[b1];
+    if (t + len > c->t_max) break;
+    t += len;
+    ++b1;
+  }
+  *tokens = t;
+  return b1;
+}
+
+// Fills the batch's metadata staging (cu_seqlens and the 64-query tile prefix into mh, the
+// 128-query attention tile records into th) and counts its visible query-key pairs.
+struct BatchMeta {
+  int q = 0;            // 64-query tiles
+  int n_tiles128 = 0;   // 128-query attention tiles (-1: a sequence too long for them)
+  double pg = 0.0;      // visible query-key pairs, global layers
+  double pl = 0.0;      // ... sliding-window layers
+};
+BatchMeta fill_batch_meta(const rv_ctx* c, const int32_t* cu, int32_t b0, int nb, int* mh, int2* th) {
+  BatchMeta m;
+  const int64_t w = c->d.local_window / 2;
+  for (int i = 0; i <= nb; ++i) {
+    mh[i] = cu[b0 + i] - cu[b0];
+    mh[nb + 1 + i] = m.q;
+    if (i < nb) {
+      const int64_t len = cu[b0 + i + 1] - cu[b0 + i];
+      m.q += static_cast<int>((len + 63) / 64);
+      m.pg += double(len) * double(len);
+      const int64_t k = std::min<int64_t>(w, len > 0 ? len - 1 : 0);
+      m.pl += double(len) + 2.0 * (double(k) * len - double(k) * (k + 1) / 2.0);
+    }
+  }
+  m.n_tiles128 = rv::fill_attention_tiles(mh, nb, th);
+  return m;
+}
+
+// Enqueues the metadata copies of one batch from the given pinned staging.
+int upload_meta(rv_ctx* c, const int* mh, const int2* th, int nb, const BatchMeta& m) {
+  if (m.n_tiles128 < 0) return fail(c, RV_E_INVALID, "sequence too long for the attention tiles");
+  RV_CUDA_TRY(c, cudaMemcpyAsync(c->meta_d, mh, sizeof(int) * 2 * (nb + 1), cudaMemcpyHostToDevice, c->stream));
+  if (m.n_tiles128 > 0)
+    RV_CUDA_TRY(c, cudaMemcpyAsync(c->tiles_d, th, sizeof(int2) * m.n_tiles128, cudaMemcpyHostToDevice,
+                                   c->stream));
+  return RV_OK;
+}
+
 template <class IdsFn, class OutFn>
 int run_batches(rv_ctx* c, const int32_t* cu, int32_t n, IdsFn ids_src, OutFn out_dst) {
   int32_t b0 = 0;
   bool first = true;
   while (b0 < n) {
-    int32_t b1 = b0;
     int64_t tokens = 0;
-    while (b1 < n && (b1 - b0) < c->n_max) {
-      const int64_t len = int64_t(cu[b1 + 1]) - cu[b1];
-      if (tokens + len > c->t_max) break;
-      tokens += len;
-      ++b1;
-    }
+    const int32_t b1 = batch_end(c, cu, n, b0, &tokens);
     const int nb = b1 - b0;
     // Staging buffer reuse: the previous batch's metadata copy must have executed.
     if (!first) RV_CUDA_TRY(c, cudaEventSynchronize(c->meta_evt));
     first = false;
-    int* mh = c->meta_h;
-    int q = 0;
-    double pg = 0.0, pl = 0.0;  // visible query-key pairs (global / sliding window)
-    const int64_t w = c->d.local_window / 2;
-    for (int i = 0; i <= nb; ++i) {
-      mh[i] = cu[b0 + i] - cu[b0];
-      mh[nb + 1 + i] = q;
-      if (i < nb) {
-        const int64_t len = cu[b0 + i + 1] - cu[b0 + i];
-        q += static_cast<int>((len + 63) / 64);
-        pg += double(len) * double(len);
-        const int64_t m = std::min<int64_t>(w, len > 0 ? len - 1 : 0);
-        pl += double(len) + 2.0 * (double(m) * len - double(m) * (m + 1) / 2.0);
-      }
-    }
-    RV_CUDA_TRY(c, cudaMemcpyAsync(c->meta_d, mh, sizeof(int) * 2 * (nb + 1),
-                                   cudaMemcpyHostToDevice, c->stream));
-    // 128-query tile records of the tcgen05 attention kernel.
-    const int n_tiles128 = rv::fill_attention_tiles(mh, nb, c->tiles_h);
-    if (n_tiles128 < 0) return fail(c, RV_E_INVALID, "sequence too long for the attention tiles");
-    if (n_tiles128 > 0)
-      RV_CUDA_TRY(c, cudaMemcpyAsync(c->tiles_d, c->tiles_h, sizeof(int2) * n_tiles128,
-                                     cudaMemcpyHostToDevice, c->stream));
+    const BatchMeta m = fill_batch_meta(c, cu, b0, nb, c->meta_h, c->tiles_h);
+    int rc = upload_meta(c, c->meta_h, c->tiles_h, nb, m);
+    if (rc) return rc;
     RV_CUDA_TRY(c, cudaEventRecord(c->meta_evt, c->stream));
     const int* ids = ids_src(b0, static_cast<int>(tokens));
     if (!ids) return RV_E_CUDA;
-    int rc = forward(c, ids, static_cast<int>(tokens), nb, q, n_tiles128, pg, pl, c->out_d);
+    rc = forward(c, ids, static_cast<int>(tokens), nb, m.q, m.n_tiles128, m.pg, m.pl, c->out_d);
     if (rc) return rc;
     if ((rc = out_dst(b0, nb, c->out_d))) return rc;
     b0 = b1;
   }
   return RV_OK;
+}
+
+// ---------------------------------------------------------------- asynchronous path
+int async_init(rv_ctx* c) {
+  if (c->aslots_ready) return RV_OK;
+  for (AsyncSlot& a : c->aslots) {
+    if (cudaMallocHost(reinterpret_cast<void**>(&a.ids_h), size_t(c->t_max) * 4) != cudaSuccess ||
+        cudaMallocHost(reinterpret_cast<void**>(&a.meta_h), size_t(2) * (c->n_max + 1) * 4) != cudaSuccess ||
+        cudaMallocHost(reinterpret_cast<void**>(&a.tiles_h), size_t(c->tiles_cap) * sizeof(int2)) != cudaSuccess ||
+        cudaMallocHost(reinterpret_cast<void**>(&a.err_h), 4) != cudaSuccess ||
+        cudaEventCreateWithFlags(&a.done, cudaEventDisableTiming) != cudaSuccess)
+      return fail(c, RV_E_NOMEM, "pinned staging for the asynchronous path could not be allocated");
+  }
+  c->aslots_ready = true;
+  return RV_OK;
+}
+
+void async_release(rv_ctx* c) {
+  for (AsyncSlot& a : c->aslots) {
+    if (a.ids_h) cudaFreeHost(a.ids_h);
+    if (a.meta_h) cudaFreeHost(a.meta_h);
+    if (a.tiles_h) cudaFreeHost(a.tiles_h);
+    if (a.out_h) cudaFreeHost(a.out_h);
+    if (a.err_h) cudaFreeHost(a.err_h);
+    if (a.done) cudaEventDestroy(a.done);
+    a = AsyncSlot{};
+  }
+  c->aslots_ready = false;
+}
+
+// Completes the oldest batch in flight: waits for its copies back, then moves its embeddings from
+// the slot's pinned staging into the caller's rows (or records the device error of its ticket).
+int async_finish_front(rv_ctx* c) {
+  const AsyncBatch b = c->inflight.front();
+  c->inflight.pop_front();
+  AsyncSlot& a = c->aslots[b.slot];
+  a.busy = false;
+  int rc = RV_OK;
+  const cudaError_t e = cudaEventSynchronize(a.done);
+  if (e != cudaSuccess) {
+    rc = fail(c, RV_E_CUDA, std::string("asynchronous batch: ") + cudaGetErrorString(e));
+  } else if (*a.err_h) {
+    std::string m = "device error flags " + std::to_string(*a.err_h);
+    if (*a.err_h & rv::kErrWaitTimeout) m += " (pipeline wait expired)";
+    if (*a.err_h & rv::kErrBadShape) m += " (token id out of range)";
+    rc = fail(c, RV_E_DEVICE, m);
+  } else {
+    std::memcpy(b.dst, a.out_h, sizeof(float) * size_t(b.nb) * c->d.hidden);
+  }
+  auto it = c->ticket_rc.find(b.ticket);
+  if (it != c->ticket_rc.end() && it->second == RV_OK) it->second = rc;
+  return rc;
 }
 
 }  // namespace
@@ -730,6 +808,7 @@ void rv_destroy(rv_ctx* c) {
     if (c->meta_h) cudaFreeHost(c->meta_h);
     if (c->tiles_h) cudaFreeHost(c->tiles_h);
     if (c->meta_evt) cudaEventDestroy(c->meta_evt);
+    async_release(c);
     for (auto& m : c->marks) {
       cudaEventDestroy(m.a);
       cudaEventDestroy(m.b);
@@ -853,6 +932,104 @@ int rv_embed_varlen_device(rv_ctx* c, const int32_t* ids_dev, const int32_t* cu,
   }
   rc = check_device_error(c);
   collect_marks(c);
+  return rc;
+}
+
+int rv_embed_submit(rv_ctx* c, const int32_t* ids, const int32_t* cu, int32_t n, float* out_host,
+                    int64_t* ticket) {
+  if (!c) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (!ticket || n < 0 || (n > 0 && (!cu || !out_host))) return fail(c, RV_E_INVALID, "null argument");
+  *ticket = 0;
+  if (!c->finalized) return fail(c, RV_E_NOT_READY, "rv_finalize has not been called");
+  int rc = RV_OK;
+  if (n > 0) {
+    if ((rc = validate_cu(c, cu, n))) return rc;
+    const int64_t total = cu[n];
+    if (total > 0 && !ids) return fail(c, RV_E_INVALID, "null ids");
+    for (int64_t t = 0; t < total; ++t)
+      if (ids[t] < 0 || ids[t] >= c->d.vocab)
+        return fail(c, RV_E_INVALID, "token id " + std::to_string(ids[t]) + " at position " + std::to_string(t) +
+                                         " is outside the vocabulary");
+  }
+  DeviceGuard g(c->device);
+  if ((rc = async_init(c))) return rc;
+  const int64_t t = c->next_ticket++;
+  c->ticket_rc[t] = RV_OK;
+  const int H = c->d.hidden;
+  int32_t b0 = 0;
+  while (b0 < n && rc == RV_OK) {
+    int64_t tokens = 0;
+    const int32_t b1 = batch_end(c, cu, n, b0, &tokens);
+    const int nb = b1 - b0;
+    // A slot is reused once its previous batch has been moved to its caller (the bounded ring:
+    // at most kAsyncSlots batches are in flight).
+    const int si = c->next_slot;
+    AsyncSlot& a = c->aslots[si];
+    while (a.busy && !c->inflight.empty()) async_finish_front(c);
+    const size_t need = size_t(nb) * H;
+    if (a.out_cap < need) {
+      if (a.out_h) cudaFreeHost(a.out_h);
+      a.out_h = nullptr;
+      a.out_cap = 0;
+      if (cudaMallocHost(reinterpret_cast<void**>(&a.out_h), need * sizeof(float)) != cudaSuccess) {
+        rc = fail(c, RV_E_NOMEM, "pinned output staging could not be allocated");
+        break;
+      }
+      a.out_cap = need;
+    }
+    const BatchMeta m = fill_batch_meta(c, cu, b0, nb, a.meta_h, a.tiles_h);
+    if ((rc = upload_meta(c, a.meta_h, a.tiles_h, nb, m))) break;
+    if (tokens > 0) {
+      std::memcpy(a.ids_h, ids + cu[b0], sizeof(int32_t) * size_t(tokens));
+      if (cudaMemcpyAsync(c->ids_d, a.ids_h, sizeof(int32_t) * size_t(tokens), cudaMemcpyHostToDevice,
+                          c->stream) != cudaSuccess) {
+        rc = fail(c, RV_E_CUDA, "ids upload failed");
+        break;
+      }
+    }
+    if ((rc = forward(c, c->ids_d, static_cast<int>(tokens), nb, m.q, m.n_tiles128, m.pg, m.pl, c->out_d))) break;
+    if (cudaMemcpyAsync(a.out_h, c->out_d, sizeof(float) * need, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync(a.err_h, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
+        cudaMemsetAsync(c->d_err, 0, 4, c->stream) != cudaSuccess ||
+        cudaEventRecord(a.done, c->stream) != cudaSuccess) {
+      rc = fail(c, RV_E_CUDA, "asynchronous batch could not be queued");
+      break;
+    }
+    a.busy = true;
+    c->inflight.push_back(AsyncBatch{si, t, out_host + size_t(b0) * H, nb});
+    c->next_slot = (si + 1) % rv_ctx::kAsyncSlots;
+    b0 = b1;
+  }
+  if (rc != RV_OK) {
+    // Nothing of a failed submission may write into the caller's buffer after this returns.
+    const std::string msg = c->err;
+    while (!c->inflight.empty()) async_finish_front(c);
+    c->ticket_rc.erase(t);
+    c->err = msg;
+    return rc;
+  }
+  *ticket = t;
+  return RV_OK;
+}
+
+int rv_embed_wait(rv_ctx* c, int64_t ticket) {
+  if (!c) return RV_E_INVALID;
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (ticket <= 0 || ticket >= c->next_ticket) return fail(c, RV_E_INVALID, "unknown ticket");
+  auto it = c->ticket_rc.find(ticket);
+  if (it == c->ticket_rc.end()) return RV_OK;  // already waited on
+  DeviceGuard g(c->device);
+  std::string msg;
+  while (!c->inflight.empty() && c->inflight.front().ticket <= ticket) {
+    const int64_t bt = c->inflight.front().ticket;
+    const int r = async_finish_front(c);
+    if (r != RV_OK && bt == ticket) msg = c->err;
+  }
+  const int rc = c->ticket_rc[ticket];
+  c->ticket_rc.erase(ticket);
+  if (c->inflight.empty()) collect_marks(c);
+  if (rc != RV_OK) c->err = msg.empty() ? c->err : msg;
   return rc;
 }
 

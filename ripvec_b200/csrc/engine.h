@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <map>
+#include <deque>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -49,6 +50,25 @@ struct LayerWeights {
 };
 
 }  // namespace rv
+
+// Pinned host staging of one in-flight batch of the asynchronous path (rv_embed_submit).
+struct AsyncSlot {
+  int32_t* ids_h = nullptr;       // [t_max] token ids
+  int* meta_h = nullptr;          // [2 (n_max + 1)] cu_seqlens and 64-query tile prefix
+  int2* tiles_h = nullptr;        // [tiles_cap] 128-query attention tile records
+  float* out_h = nullptr;         // [out_cap] embeddings of the batch
+  size_t out_cap = 0;
+  unsigned int* err_h = nullptr;  // the device error word after the batch
+  cudaEvent_t done = nullptr;     // recorded after the batch's copies back
+  bool busy = false;
+};
+// A batch queued by rv_embed_submit whose results still sit in its slot.
+struct AsyncBatch {
+  int slot;
+  int64_t ticket;
+  float* dst;  // caller's rows for this batch
+  int nb;
+};
 
 struct rv_ctx {
   rv_model_desc d{};
@@ -100,6 +120,16 @@ struct rv_ctx {
   bool attn_tc = true;                   // tcgen05 attention for head_dim 64 (RV_ATTN_TC=0 turns off)
 
   std::vector<void*> allocations;
+
+  // asynchronous path (rv_embed_submit / rv_embed_wait): two slots of pinned staging, batches in
+  // flight in submission order, and the status of tickets not yet waited on.
+  static constexpr int kAsyncSlots = 2;
+  AsyncSlot aslots[kAsyncSlots];
+  bool aslots_ready = false;
+  std::deque<AsyncBatch> inflight;
+  int next_slot = 0;
+  int64_t next_ticket = 1;
+  std::map<int64_t, int> ticket_rc;  // tickets submitted and not yet waited on -> status
 
   // per-kernel profiling (rv_set_profiling)
   bool profiling = false;

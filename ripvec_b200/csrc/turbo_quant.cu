@@ -150,11 +150,12 @@ __global__ void __launch_bounds__(128) polar_lut_kernel(const float* __restrict_
 }
 
 // ---------------------------------------------------------------- scan
-// Threads per scan CTA: the 4-query tables (4 x 24 KB at 768 dims) allow two CTAs per SM, so
-// that variant runs 16 warps per CTA to keep 32 warps of loads in flight per SM.
+// Threads per scan CTA: the 4-query tables (4 x 24 KB at 768 dims) allow two CTAs per SM and the
+// 8-query tables (192 KB) one, so those variants run 16 and 32 warps per CTA to keep 32 warps of
+// loads in flight per SM.
 template <int QB>
 constexpr int scan_threads() {
-  return QB == 4 ? 512 : 256;
+  return QB == 8 ? 1024 : QB == 4 ? 512 : 256;
 }
 
 // QB consecutive table entries (queries q0..q0+QB-1 of one pair and bin) in one shared load.
@@ -180,6 +181,21 @@ struct QVec<4> {
     v[1] = t.y;
     v[2] = t.z;
     v[3] = t.w;
+  }
+};
+template <>
+struct QVec<8> {
+  __device__ __forceinline__ static void get(const float* p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x;
+    v[1] = a.y;
+    v[2] = a.z;
+    v[3] = a.w;
+    v[4] = b.x;
+    v[5] = b.y;
+    v[6] = b.z;
+    v[7] = b.w;
   }
 };
 
@@ -364,7 +380,7 @@ __global__ void sel_all_kernel(int64_t n, int64_t row_base, int pre, int nq, int
 
 int scan_qb(int pairs, int levels, int qn) {
   const size_t tab = size_t(pairs) * levels * sizeof(float);
-  int qb = 4;
+  int qb = 8;
   while (qb > 1 && (qb > qn || tab * qb > kPolarMaxLutBytes)) qb >>= 1;
   return qb;
 }
@@ -444,7 +460,10 @@ cudaError_t polar_scan(const float* radii, const uint8_t* bins, int pairs, int64
     // scan_qb never exceeds the queries left, so every pass scores exactly qb queries.
     const int qb = scan_qb(pairs, levels, nq - q0);
     cudaError_t e;
-    if (qb == 4)
+    if (qb == 8)
+      e = launch_scan<8>(radii, bins, pairs, g_begin, g_count, rows, lut + q0 * tab, levels, s + q0 * ld, ld, sms,
+                         st);
+    else if (qb == 4)
       e = launch_scan<4>(radii, bins, pairs, g_begin, g_count, rows, lut + q0 * tab, levels, s + q0 * ld, ld, sms,
                          st);
     else if (qb == 2)

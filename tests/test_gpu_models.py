@@ -246,3 +246,34 @@ def test_kernel_variants_agree(base_weights, monkeypatch, env):
     assert row_cosines(outs[0], outs[1]).min() >= 0.9999
     ref = modern_bert.embed_batch(base_weights, modern_cfg(MODERNBERT_BASE), ids, cu)
     assert row_cosines(outs[0], ref).min() >= COS_BF16
+
+
+def test_async_submit_wait_matches_the_synchronous_call(tiny_modern):
+    """rv_embed_submit / rv_embed_wait: several jobs queued before any wait, each cut into many
+    batches by a small token budget so the two pinned staging slots are reused across jobs, give
+    the same embeddings as rv_embed_varlen; a synchronous call between submit and wait is ordered
+    correctly; a bad token id fails at submit; an unknown ticket is an error."""
+    g, w = tiny_modern
+    be = EmbedBackend(TINY_MODERN, w, dtype="bf16", max_batch_tokens=2048)
+    jobs = []
+    for s in range(4):
+        lengths = synth.uniform_lengths(60 + 10 * s, 1, 600, seed=40 + s)
+        ids, cu = synth.packed_ids(lengths, TINY_MODERN.vocab, seed=50 + s)
+        jobs.append((ids, cu, be.embed_packed(ids, cu)))
+    tickets = [be.submit(ids, cu) for ids, cu, _ in jobs]
+    mid = be.embed_packed(jobs[1][0], jobs[1][1])  # synchronous call while jobs are in flight
+    np.testing.assert_array_equal(mid, jobs[1][2])
+    for (ticket, out), (_, _, expect) in zip(tickets[::-1], jobs[::-1]):
+        be.wait(ticket)  # the last ticket first: every earlier one completes with it
+        np.testing.assert_array_equal(out, expect)
+    be.wait(tickets[0][0])  # waiting twice is fine
+    bad = jobs[0][0].copy()
+    bad[3] = TINY_MODERN.vocab
+    with pytest.raises(RvError):
+        be.submit(bad, jobs[0][1])
+    with pytest.raises(RvError):
+        be.wait(10_000)
+    t, out = be.submit(jobs[2][0], jobs[2][1])
+    be.wait(t)
+    np.testing.assert_array_equal(out, jobs[2][2])
+    be.close()

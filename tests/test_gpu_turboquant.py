@@ -26,7 +26,7 @@ def corpus():
 @pytest.fixture(scope="module")
 def queries(corpus):
     db = corpus[0]
-    q = synth.normalized_gaussian(7, db.shape[1], seed=32)  # 7 = scan batches of 4 + 2 + 1
+    q = synth.normalized_gaussian(15, db.shape[1], seed=32)  # 15 = scan batches of 8 + 4 + 2 + 1
     q[4] = db[11]
     return q
 
