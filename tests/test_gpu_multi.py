@@ -48,7 +48,7 @@ def test_embed_distributed_matches_one_context(cuda_device):
 
 
 def _sharded(torch, db, q, k, base, comm, threshold=float("-inf")):
-    idx = SearchIndex(db, base=base)
+    idx = SearchIndex(db, base=base, device=comm.device)
     qd = torch.from_numpy(q).cuda()
     oi = torch.empty(len(q), k, dtype=torch.int64, device="cuda")
     os_ = torch.empty(len(q), k, dtype=torch.float32, device="cuda")
