@@ -132,18 +132,22 @@ __device__ __forceinline__ float masked_max(float (&s)[32], int cls, int kb, int
 template <typename T>
 __device__ __forceinline__ void make_p(bool live, const float (&s)[32], uint64_t sl2, uint64_t nm2,
                                        uint64_t (&ps)[2], uint32_t (&w)[16]) {
+  // One branch for the whole half (not one per pair), so the 32 exponentials form a single
+  // basic block that the compiler can interleave.
+  if (!live) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) w[e] = 0u;
+    return;
+  }
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
-    w[e] = 0u;
-    if (live) {
-      // Masked scores are -inf: exp2(-inf) = 0 exactly.
-      float x0, x1;
-      f2_unpack(f2_fma(f2_pack(s[2 * e], s[2 * e + 1]), sl2, nm2), x0, x1);
-      const float p0 = ex2(x0), p1 = ex2(x1);
-      ps[e & 1] = f2_add(ps[e & 1], f2_pack(p0, p1));
-      auto v = Elem<T>::pack(p0, p1);
-      w[e] = *reinterpret_cast<uint32_t*>(&v);
-    }
+    // Masked scores are -inf: exp2(-inf) = 0 exactly.
+    float x0, x1;
+    f2_unpack(f2_fma(f2_pack(s[2 * e], s[2 * e + 1]), sl2, nm2), x0, x1);
+    const float p0 = ex2(x0), p1 = ex2(x1);
+    ps[e & 1] = f2_add(ps[e & 1], f2_pack(p0, p1));
+    auto v = Elem<T>::pack(p0, p1);
+    w[e] = *reinterpret_cast<uint32_t*>(&v);
   }
 }
 
