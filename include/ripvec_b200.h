@@ -290,9 +290,12 @@ int rv_index_rank_cascade(rv_index* idx, const float* queries, int32_t nq, int32
  * whose exact score (as rv_index_topk: sequential f64 sum of the bf16 products) is >= threshold,
  * ordered by (score desc, a asc, b asc), at most max_pairs of them.  Fewer than two rows give no
  * pairs.  Rows are numbered base + local row.  out_a / out_b [max_pairs] int64, out_score
- * [max_pairs] f32, out_score64 (optional) f64, *out_count = pairs written; host buffers.  At
- * most 8388608 pairs may score within the f32 error bound of the threshold (about
- * dim * 2^-22 for unit rows); more returns RV_E_DEVICE (raise the threshold). */
+ * [max_pairs] f32, out_score64 (optional) f64, *out_count = pairs written; host buffers.  One
+ * pass keeps up to 8388608 candidate pairs (f32 score within the error bound, about
+ * dim * 2^-22 for unit rows, of the cut).  When more reach the threshold's bound, the cut is
+ * raised by bisection, one pass per step, until the candidates fit and at least max_pairs pairs
+ * reach the cut; RV_E_DEVICE only when no cut does (more than 8388608 pairs within the bound
+ * of the max_pairs-th best score, or of the threshold itself). */
 int rv_index_find_duplicates(rv_index* idx, float threshold, int64_t max_pairs, int64_t* out_a, int64_t* out_b,
                              float* out_score, double* out_score64, int64_t* out_count);
 

@@ -872,56 +872,84 @@ int rv_index_find_duplicates(rv_index* x, float threshold, int64_t max_pairs, in
   Dev g(x->device);
   cudaStream_t st = x->stream;
   const int n = static_cast<int>(x->n), dim = x->dim;
-  // Candidate bound: every pair whose exact score reaches the threshold has an f32 tensor-core
-  // score of at least threshold - eps.
+  // Candidate bound: every pair whose exact score reaches a cut c has an f32 tensor-core score of
+  // at least c - eps.
   const double eps = double(dim) * std::ldexp(1.0, -22) * x->max_norm * x->max_norm;
-  const float thr_lo = std::nextafter(static_cast<float>(double(threshold) - eps), -INFINITY);
-  constexpr long long kCap = 1LL << 23;  // candidate records per call (16 bytes each)
-  int strip = 16384;                     // rows per GEMM launch (RV_DUP_STRIP_ROWS for tests)
+  long long cap = 1LL << 23;  // candidate records per pass (16 bytes each; RV_DUP_CAP_RECORDS for tests)
+  if (const char* e = std::getenv("RV_DUP_CAP_RECORDS")) cap = std::max(1024LL, std::atoll(e));
+  int strip = 16384;          // rows per GEMM launch (RV_DUP_STRIP_ROWS for tests)
   if (const char* e = std::getenv("RV_DUP_STRIP_ROWS")) strip = std::max(128, std::atoi(e) / 128 * 128);
-  if (!x->dup_rec.reserve(size_t(kCap)) || !x->dup_cnt.reserve(1))
+  if (!x->dup_rec.reserve(size_t(cap)) || !x->dup_cnt.reserve(1))
     return ifail(x, RV_E_NOMEM, "duplicate candidate buffer allocation failed");
-  IX_TRY(x, cudaMemsetAsync(x->dup_cnt.p, 0, sizeof(unsigned long long), st));
-  for (int r0 = 0; r0 < n; r0 += strip) {
-    const int rows = std::min(strip, n - r0);
-    const int cols = (n - r0 + 255) / 256 * 256;
-    CUtensorMap ts;
-    std::string why;
-    if (!rv::make_tmap_2d_16bit(&ts, x->db + size_t(r0) * dim, true, dim, uint64_t(rows), uint64_t(dim) * 2, 64,
-                                128, &why))
-      return ifail(x, RV_E_CUDA, why);
-    IX_TRY(x, rv::dup_candidates(ts, x->tmap_db, rows, cols, dim, r0, n, thr_lo, x->dup_rec.p, x->dup_cnt.p, kCap,
-                                 x->d_err, st));
-    x->launches++;
-  }
-  unsigned long long m = 0;
-  unsigned int e = 0;
-  IX_TRY(x, cudaMemcpyAsync(&m, x->dup_cnt.p, sizeof(m), cudaMemcpyDeviceToHost, st));
-  IX_TRY(x, cudaMemcpyAsync(&e, x->d_err, 4, cudaMemcpyDeviceToHost, st));
-  IX_TRY(x, cudaStreamSynchronize(st));
-  if (e) {
-    cudaMemset(x->d_err, 0, 4);
-    return ifail(x, RV_E_DEVICE, "duplicate search kernel reported device error flags " + std::to_string(e));
-  }
-  if (m > static_cast<unsigned long long>(kCap))
-    return ifail(x, RV_E_DEVICE,
-                 std::to_string(m) + " pairs score within the error bound of the threshold (more than " +
-                     std::to_string(kCap) + "); raise the threshold");
-  std::vector<int4> rec(m);
-  std::vector<double> s64(m);
-  if (m > 0) {
-    if (!x->dup_s64.reserve(size_t(m))) return ifail(x, RV_E_NOMEM, "duplicate score buffer allocation failed");
-    IX_TRY(x, rv::dup_rescore(x->db, dim, x->dup_rec.p, static_cast<long long>(m), x->dup_s64.p, st));
-    x->launches++;
-    IX_TRY(x, cudaMemcpyAsync(rec.data(), x->dup_rec.p, sizeof(int4) * m, cudaMemcpyDeviceToHost, st));
-    IX_TRY(x, cudaMemcpyAsync(s64.data(), x->dup_s64.p, sizeof(double) * m, cudaMemcpyDeviceToHost, st));
+  // One pass over the upper triangle: the candidates of cut c into dup_rec, their count into m
+  // (more than cap: the buffer overflowed and holds an arbitrary subset).
+  auto pass = [&](double c, unsigned long long& m) -> int {
+    const float thr_lo = std::nextafter(static_cast<float>(c - eps), -INFINITY);
+    IX_TRY(x, cudaMemsetAsync(x->dup_cnt.p, 0, sizeof(unsigned long long), st));
+    for (int r0 = 0; r0 < n; r0 += strip) {
+      const int rows = std::min(strip, n - r0);
+      const int cols = (n - r0 + 255) / 256 * 256;
+      CUtensorMap ts;
+      std::string why;
+      if (!rv::make_tmap_2d_16bit(&ts, x->db + size_t(r0) * dim, true, dim, uint64_t(rows), uint64_t(dim) * 2, 64,
+                                  128, &why))
+        return ifail(x, RV_E_CUDA, why);
+      IX_TRY(x, rv::dup_candidates(ts, x->tmap_db, rows, cols, dim, r0, n, thr_lo, x->dup_rec.p, x->dup_cnt.p, cap,
+                                   x->d_err, st));
+      x->launches++;
+    }
+    unsigned int e = 0;
+    IX_TRY(x, cudaMemcpyAsync(&m, x->dup_cnt.p, sizeof(m), cudaMemcpyDeviceToHost, st));
+    IX_TRY(x, cudaMemcpyAsync(&e, x->d_err, 4, cudaMemcpyDeviceToHost, st));
     IX_TRY(x, cudaStreamSynchronize(st));
+    if (e) {
+      cudaMemset(x->d_err, 0, 4);
+      return ifail(x, RV_E_DEVICE, "duplicate search kernel reported device error flags " + std::to_string(e));
+    }
+    return RV_OK;
+  };
+  // The threshold first.  When more than cap candidates fall within the error bound of it, the
+  // best max_pairs pairs lie above a higher cut: bisect the cut between the last value that
+  // overflowed and the largest possible score until a pass fits and keeps at least max_pairs
+  // exact pairs (every pair below such a cut ranks after all of them).  The reference scores
+  // the whole n x n matrix and keeps the best max_pairs whatever their number.
+  double cut = double(threshold), lo_c = double(threshold), hi_c = x->max_norm * x->max_norm + eps;
+  unsigned long long m = 0;
+  std::vector<int4> rec;
+  std::vector<double> s64;
+  for (int it = 0;; ++it) {
+    if (const int rc = pass(cut, m)) return rc;
+    const bool over = m > static_cast<unsigned long long>(cap);
+    size_t kept = 0;
+    if (!over) {
+      rec.resize(m);
+      s64.resize(m);
+      if (m > 0) {
+        if (!x->dup_s64.reserve(size_t(m))) return ifail(x, RV_E_NOMEM, "duplicate score buffer allocation failed");
+        IX_TRY(x, rv::dup_rescore(x->db, dim, x->dup_rec.p, static_cast<long long>(m), x->dup_s64.p, st));
+        x->launches++;
+        IX_TRY(x, cudaMemcpyAsync(rec.data(), x->dup_rec.p, sizeof(int4) * m, cudaMemcpyDeviceToHost, st));
+        IX_TRY(x, cudaMemcpyAsync(s64.data(), x->dup_s64.p, sizeof(double) * m, cudaMemcpyDeviceToHost, st));
+        IX_TRY(x, cudaStreamSynchronize(st));
+      }
+      for (size_t t = 0; t < m; ++t) kept += s64[t] >= cut;
+      if (cut == double(threshold) || kept >= size_t(max_pairs)) break;
+      hi_c = cut;  // too few pairs above this cut: lower it
+    } else {
+      lo_c = cut;  // too many candidates: raise it
+    }
+    const double next = 0.5 * (lo_c + hi_c);
+    if (it >= 60 || !(next > lo_c && next < hi_c))
+      return ifail(x, RV_E_DEVICE,
+                   "more than " + std::to_string(cap) + " pairs score within the f32 error bound of every cut " +
+                       "that keeps " + std::to_string(max_pairs) + " pairs; raise the threshold");
+    cut = next;
   }
   // Keep exact scores >= threshold; order (score desc, a asc, b asc); the best max_pairs.
   std::vector<size_t> keep;
   keep.reserve(m);
   for (size_t t = 0; t < m; ++t)
-    if (s64[t] >= double(threshold)) keep.push_back(t);
+    if (s64[t] >= cut) keep.push_back(t);
   auto before = [&](size_t u, size_t v) {
     if (s64[u] != s64[v]) return s64[u] > s64[v];
     if (rec[u].x != rec[v].x) return rec[u].x < rec[v].x;

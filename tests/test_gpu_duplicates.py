@@ -1,13 +1,16 @@
 """All-pairs near-duplicate search (``SearchIndex::find_duplicates``, ``index.rs:325-348``) on the
 GPU through the C ABI, bit-exact against the oracle (``oracle/scan.py:find_duplicates``): pairs,
 order and f64 scores, at the reference's default threshold and at a low threshold with thousands of
-pairs, across strip boundaries of the tensor-core GEMM, with a row offset, and the empty cases."""
+pairs, across strip boundaries of the tensor-core GEMM, with a row offset, and the empty cases.
+When more candidates reach the threshold than one pass keeps, the cut is raised until the best
+max_pairs fit (checked with a small test capacity, ``RV_DUP_CAP_RECORDS``)."""
 
 import numpy as np
 import pytest
 
 from oracle import scan
 from ripvec_b200 import synth
+from ripvec_b200._lib import RvError
 from ripvec_b200.index import SearchIndex
 
 pytestmark = pytest.mark.gpu
@@ -65,3 +68,34 @@ def test_dim_768_and_empty_cases(cuda_device):
     assert res[0][:2] == (3, 700) and all(x < y for x, y, _ in res)
     assert SearchIndex(db[:1]).find_duplicates(0.0, 10) == []
     assert idx.find_duplicates(0.5, 0) == []
+
+
+@pytest.fixture(scope="module")
+def crowded():
+    """600 rows: 300 noisy copies of one direction (44,850 pairs between 0.9 and 1) and 300
+    unrelated rows."""
+    dim = 128
+    rng = np.random.default_rng(60)
+    c = rng.standard_normal(dim).astype(np.float32)
+    near = c + 0.25 * rng.standard_normal((300, dim)).astype(np.float32)
+    db = np.concatenate([near, synth.normalized_gaussian(300, dim, seed=61)])
+    return (db / np.linalg.norm(db, axis=1, keepdims=True)).astype(np.float32)
+
+
+@pytest.mark.parametrize("max_pairs", [20, 1000])
+def test_overflowing_threshold_raises_the_cut(cuda_device, crowded, monkeypatch, max_pairs):
+    monkeypatch.setenv("RV_DUP_CAP_RECORDS", "2048")  # far fewer than the 44,850 crowded pairs
+    want = scan.find_duplicates(crowded, 0.5, max_pairs)
+    assert len(want[0]) == max_pairs
+    check(SearchIndex(crowded).duplicate_pairs(0.5, max_pairs), want)
+
+
+def test_no_cut_fits_is_an_error(cuda_device, monkeypatch):
+    monkeypatch.setenv("RV_DUP_CAP_RECORDS", "2048")
+    db = np.repeat(synth.normalized_gaussian(1, 128, seed=62), 300, axis=0)  # 44,850 pairs at 1.0
+    idx = SearchIndex(db)
+    with pytest.raises(RvError):
+        idx.duplicate_pairs(0.5, 20)
+    monkeypatch.setenv("RV_DUP_CAP_RECORDS", "65536")  # the same index, with room for every pair
+    a, b, s, _ = idx.duplicate_pairs(0.5, 20)
+    assert len(a) == 20 and (a[0], b[0]) == (0, 1)
