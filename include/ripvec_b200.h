@@ -285,6 +285,23 @@ int rv_index_cascade_rows(rv_index* idx, float* out);
 int rv_index_rank_cascade(rv_index* idx, const float* queries, int32_t nq, int32_t top_k, float threshold,
                           int64_t* out_idx, float* out_score, double* out_score64, int32_t* out_count);
 
+/* ---------------------------------------------------------------- embedding store */
+/* The embeddings of one per-file cache object (crates/ripvec-core/src/cache/file_cache.rs:15-70,
+ * read back by cache/reindex.rs:302, :411): a zstd frame around an rkyv 0.8 archive of
+ * FileCache { chunks, embeddings: [n x hidden_dim] f32, hidden_dim }, or the bare archive.
+ * Host-only (no device needed).  Rows: the chunks whose whole embedding slice is present,
+ * min(chunks, len(embeddings) / hidden_dim) (cache/reindex.rs:578-587).  out_emb = NULL: only
+ * *out_rows and *out_dim = hidden_dim are set; else rows * hidden_dim floats go to out_emb
+ * (capacity_floats at least that).  Objects starting with "BC" (the portable bitcode form,
+ * FileCache::to_portable_bytes) and malformed objects return RV_E_IO; the message is
+ * rv_cache_last_error() (per thread).  zstd is the system's libzstd.so.1. */
+int rv_cache_decode(const uint8_t* obj, uint64_t nbytes, float* out_emb, int64_t capacity_floats, int64_t* out_rows,
+                    int32_t* out_dim);
+const char* rv_cache_last_error(void);
+/* Rows [row0, row0 + n) of an index, as stored (RV_DTYPE_BF16) or widened to f32 (exact), into a
+ * host or device buffer: the export side of a device shard (rv_index_create reads it back). */
+int rv_index_export(rv_index* idx, int64_t row0, int64_t n, int32_t dst_dtype, void* dst, int32_t dst_on_device);
+
 /* ---------------------------------------------------------------- near-duplicate pairs */
 /* SearchIndex::find_duplicates (crates/ripvec-core/src/index.rs:325-348): the pairs (a, b), a < b,
  * whose exact score (as rv_index_topk: sequential f64 sum of the bf16 products) is >= threshold,

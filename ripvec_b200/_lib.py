@@ -112,6 +112,9 @@ SIGNATURES = {
     "rv_index_cascade_rows": (C.c_int, [vp, vp]),
     "rv_index_rank_cascade": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_index_find_duplicates": (C.c_int, [vp, f32, i64, vp, vp, vp, vp, vp]),
+    "rv_cache_decode": (C.c_int, [vp, C.c_uint64, vp, i64, C.POINTER(i64), C.POINTER(i32)]),
+    "rv_cache_last_error": (C.c_char_p, []),
+    "rv_index_export": (C.c_int, [vp, i64, i64, i32, vp, i32]),
     "rv_op_gemm": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "rv_op_attention": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, f32, vp]),
     "rv_debug_stall_attention": (C.c_int, [i32, i64]),

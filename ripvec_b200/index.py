@@ -88,6 +88,18 @@ class SearchIndex:
         if rc != L.RV_OK:
             raise L.RvError(rc, self._lib.rv_index_last_error(self._h).decode())
 
+    def __len__(self) -> int:
+        return int(self._lib.rv_index_size(self._h))
+
+    def export_rows(self, row0: int = 0, n: int | None = None, bf16_bits: bool = False) -> np.ndarray:
+        """Rows ``[row0, row0 + n)`` as stored on the device (``rv_index_export``): widened to f32
+        (exact), or with ``bf16_bits`` the raw bf16 values as uint16."""
+        n = len(self) - row0 if n is None else n
+        out = np.empty((max(n, 0), self.hidden_dim), np.uint16 if bf16_bits else np.float32)
+        dt = L.RV_DTYPE_BF16 if bf16_bits else L.RV_DTYPE_F32
+        self._check(self._lib.rv_index_export(self._h, row0, n, dt, out.ctypes.data if out.size else None, 0))
+        return out
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             self._lib.rv_index_destroy(self._h)
