@@ -297,33 +297,95 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_reference_scan(args):
+def cpu_scan_baseline(n_rows, dim, steps=1, warmup=0):
+    """The reference's exact search (``rank``: f32 GEMV + full sort, ``index.rs:172-186``) on the
+    host cores over a 200k-row sample, scaled to ``n_rows``: (queries/s, ms per sampled step,
+    cpu_baseline dict)."""
     from oracle import scan as oscan
     from ripvec_b200 import synth
 
-    n_rows, dim, nq = 10_000_000, 768, 1024
     cores = pin_blas_threads()
-    # bounded sample: the reference algorithm (f32 GEMV + full sort) over a slice of the database
     sample = 200_000
     db = synth.normalized_gaussian(sample, dim, seed=77)
     q = synth.normalized_gaussian(8, dim, seed=78)
     times = []
-    for s in range(args.warmup + args.steps):
+    for s in range(warmup + steps):
         t0 = time.perf_counter()
         for qi in range(q.shape[0]):
             oscan.rank(db, q[qi], -1.0)
-        dt = time.perf_counter() - t0
-        if s >= args.warmup:
-            times.append(dt)
-    per_q_row = sum(times) / (args.steps * q.shape[0] * sample)
-    qps = 1.0 / (per_q_row * n_rows)
+        if s >= warmup:
+            times.append(time.perf_counter() - t0)
+    qps = 1.0 / (sum(times) / (steps * q.shape[0] * sample) * n_rows)
+    return qps, 1e3 * sum(times) / steps, {
+        "value": qps, "unit": "queries/s", "cores": cores, "kind": "port",
+        "sample": f"{q.shape[0]} queries x {sample} rows per step (f32 GEMV + full sort), scaled to {n_rows} rows"}
+
+
+def cpu_turboquant_baseline(n_rows, dim, top_k):
+    """``rank_turboquant`` (``index.rs:196-234``: LUT scan of the codes, top 10·top_k, exact
+    re-rank) by the oracle port on a 20k-row sample with its codes built beforehand (index build,
+    untimed), the per-query time scaled by rows."""
+    from oracle import turbo_quant as otq
+    from ripvec_b200 import synth
+
+    cores = pin_blas_threads()
+    sample = 20_000
+    rows = synth.normalized_gaussian(sample, dim, seed=81)
+    rot = otq.generate_rotation(dim, 42)
+    codes = otq.encode(rows, rot)
+    q = synth.normalized_gaussian(4, dim, seed=82)
+    t0 = time.perf_counter()
+    for qi in range(q.shape[0]):
+        otq.rank_turboquant(rows, q[qi], top_k, float("-inf"), rot, codes=codes)
+    per_q = (time.perf_counter() - t0) / q.shape[0] * (n_rows / sample)
+    return {"value": 1.0 / per_q, "unit": "queries/s", "cores": cores, "kind": "port",
+            "sample": f"{q.shape[0]} queries x {sample} rows (codes built untimed), scaled to {n_rows} rows"}
+
+
+def cpu_cascade_baseline(n_rows, dim, t_dim, top_k):
+    """``rank_cascade``'s query work (``index.rs:245-297``) in the reference's f32 arithmetic on a
+    100k-row sample whose truncated matrix is built beforehand (untimed), scaled by rows."""
+    from oracle import scan as oscan
+    from ripvec_b200 import synth
+
+    cores = pin_blas_threads()
+    sample = 100_000
+    rows = synth.normalized_gaussian(sample, dim, seed=83)
+    tr = oscan.ln_truncate(rows, t_dim)
+    q = synth.normalized_gaussian(8, dim, seed=84)
+    t0 = time.perf_counter()
+    for qi in range(q.shape[0]):
+        oscan.rank_cascade_f32(rows, tr, q[qi], top_k, float("-inf"), t_dim)
+    per_q = (time.perf_counter() - t0) / q.shape[0] * (n_rows / sample)
+    return {"value": 1.0 / per_q, "unit": "queries/s", "cores": cores, "kind": "port",
+            "sample": f"{q.shape[0]} queries x {sample} rows (truncated matrix built untimed), scaled to {n_rows} rows"}
+
+
+def cpu_duplicates_baseline(dim):
+    """``find_duplicates`` in the reference's arithmetic (f32 BLAS similarity matrix, upper
+    triangle, threshold, sort) over a 16k-row sample: pair scores per second."""
+    from oracle import scan as oscan
+    from ripvec_b200 import synth
+
+    cores = pin_blas_threads()
+    sample = 16_384
+    rows = synth.normalized_gaussian(sample, dim, seed=85)
+    t0 = time.perf_counter()
+    oscan.find_duplicates_f32(rows, 0.85, 20)
+    pps = sample * (sample - 1) / 2 / (time.perf_counter() - t0)
+    return {"value": pps, "unit": "pairs/s", "cores": cores, "kind": "port",
+            "sample": f"{sample} rows ({sample * (sample - 1) // 2} pairs), f32 BLAS upper triangle"}
+
+
+def run_reference_scan(args):
+    n_rows, dim, nq = 10_000_000, 768, 1024
+    qps, ms, base = cpu_scan_baseline(n_rows, dim, args.steps, args.warmup)
     line = {"metric": "exact cosine top-100 queries/sec (10M x 768 bf16)", "value": qps, "unit": "queries/s",
             "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * sum(times) / args.steps, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic normalised Gaussian rows",
             "config": {"workload": "scan_topk", "rows": n_rows, "dim": dim, "queries": nq},
-            "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": cores, "kind": "port",
-                             "sample": f"{q.shape[0]} queries x {sample} rows per step, scaled to {n_rows} rows"},
+            "cpu_baseline": base,
             "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -644,8 +706,16 @@ def run_scan(args):
     stream = torch.cuda.current_stream()
     # The database shard (15.4 GB at 10M rows on one GPU) is larger than L2, so every step
     # streams it from HBM: no flush is needed between steps.
-    for nq in [int(v) for v in str(args.queries).split(",")]:
-        scan_line(args, torch, dist, idx, comm, synth, stream, rank, world, local, n_rows, dim, nq, k)
+    lines = [scan_line(args, torch, dist, idx, comm, synth, stream, rank, world, local, n_rows, dim, nq, k)
+             for nq in [int(v) for v in str(args.queries).split(",")]]
+    # The CPU sample runs after every GPU measurement, so it cannot disturb one.  One query at a
+    # time on the CPU: the same baseline for every batch size.
+    if rank == 0:
+        cpu_base = None if world > 1 or args.no_cpu_baseline else cpu_scan_baseline(n_rows, dim)[2]
+        for line in lines:
+            if cpu_base is not None:
+                line["cpu_baseline"] = cpu_base
+            print(json.dumps(line), flush=True)
     if comm is not None:
         comm.close()
     idx.close()
@@ -654,7 +724,8 @@ def run_scan(args):
 
 
 def scan_line(args, torch, dist, idx, comm, synth, stream, rank, world, local, n_rows, dim, nq, k):
-    """Times ``args.steps`` exact top-k steps of ``nq`` queries and prints one JSON line (rank 0).
+    """Times ``args.steps`` exact top-k steps of ``nq`` queries and returns the JSON line (rank 0;
+    None on the other ranks).
     With several ranks a step is ``rv_index_topk_sharded``: the shard's top-k, the library's
     NCCL all-gather of the lists and the device merge."""
     from ripvec_b200.index import topk_sharded
@@ -680,19 +751,47 @@ def scan_line(args, torch, dist, idx, comm, synth, stream, rank, world, local, n
     if rank == 0:
         sampler.start()
         time.sleep(0.3)
+    launches0 = idx.kernel_launches()
     for s in range(args.steps):
         evs[s][0].record(stream)
         step()
         evs[s][1].record(stream)
     torch.cuda.synchronize()
+    launches = idx.kernel_launches() - launches0
     clocks = sampler.stop() if rank == 0 else None
     ms = sum(a.elapsed_time(b) for a, b in evs)
+    # End to end with host buffers: host queries in, host results out, host clock per step.  One
+    # GPU: the public host-buffer call (rv_index_topk).  Several: pinned copies around the
+    # sharded call, every rank timing its own steps (max over ranks below).
+    qh = synth.normalized_gaussian(nq, dim, seed=99)
+    e2e_t = []
+    if comm is None:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            idx.topk(qh, k, with_f64=True)
+            e2e_t.append(time.perf_counter() - t0)
+        d2h = nq * k * (8 + 4 + 8) + nq * 4
+    else:
+        qp = torch.from_numpy(qh).pin_memory()
+        oi_h = torch.empty(nq, k, dtype=torch.int64).pin_memory()
+        o64_h = torch.empty(nq, k, dtype=torch.float64).pin_memory()
+        dist.barrier()
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            q.copy_(qp, non_blocking=True)
+            step()
+            oi_h.copy_(oi, non_blocking=True)
+            o64_h.copy_(o64, non_blocking=True)
+            stream.synchronize()
+            e2e_t.append(time.perf_counter() - t0)
+        d2h = nq * k * (8 + 8)
+    e2e_ms = 1e3 * sum(e2e_t) / len(e2e_t)
     if dist is not None:
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, e2e_ms = float(t[0].item()), float(t[1].item())
     if rank != 0:
-        return
+        return None
     pk = peaks()
     db_bytes = (n_rows // world) * dim * 2
     line = {"metric": "exact cosine top-100 queries/sec (10M x 768 bf16)", "value": nq * args.steps / (ms / 1e3),
@@ -702,7 +801,11 @@ def scan_line(args, torch, dist, idx, comm, synth, stream, rank, world, local, n
             "config": {"workload": "scan_topk", "rows": n_rows, "dim": dim, "queries": nq, "k": k,
                        "parallelism": f"rows{world}", "l2": "database shard larger than L2, no flush"},
             "db_gbs_per_rank": db_bytes / (ms / args.steps / 1e3) / 1e9, "hbm_peak_gbs": pk["hbm_gbs"],
-            "clocks": clocks}
+            "clocks": clocks, "gpu_launches": launches,
+            "e2e": {"value": nq / (e2e_ms / 1e3), "unit": "queries/s", "h2d_bytes_per_step": nq * dim * 4,
+                    "d2h_bytes_per_step": d2h,
+                    "how": "rv_index_topk with host queries and results" if comm is None else
+                           "pinned host copies around rv_index_topk_sharded, host clock, max over ranks"}}
     # Every database byte feeds nq / 2 multiply-adds.  Above the ridge point (peak FLOP/s over
     # HBM bytes/s, about 213 FLOP per byte here, i.e. ~210 queries) the scan is bound by the
     # tensor cores (2 * nq * rows * dim FLOP per step per rank); below it by streaming the
@@ -722,7 +825,7 @@ def scan_line(args, torch, dist, idx, comm, synth, stream, rank, world, local, n
                             "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
                             "peak_source": f"{pk['source']} hbm_gbs", "traffic": None,
                             "bytes_per_step": db_bytes}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def run_turboquant(args):
@@ -752,8 +855,10 @@ def run_turboquant(args):
     build_s = time.perf_counter() - t0
     stream = torch.cuda.current_stream()
     pk = peaks()
+    lines = []
     for nq in [int(v) for v in str(args.queries).split(",")]:
-        q = torch.from_numpy(synth.normalized_gaussian(nq, dim, seed=99)).cuda()
+        qh = synth.normalized_gaussian(nq, dim, seed=99)
+        q = torch.from_numpy(qh).cuda()
         oi = torch.empty(nq, top_k, dtype=torch.int64, device="cuda")
         os_ = torch.empty(nq, top_k, dtype=torch.float32, device="cuda")
 
@@ -768,13 +873,22 @@ def run_turboquant(args):
         sampler = ClockSampler(physical_gpu(local))
         sampler.start()
         time.sleep(0.3)
+        launches0 = idx.kernel_launches()
         for st in range(args.steps):
             evs[st][0].record(stream)
             step()
             evs[st][1].record(stream)
         torch.cuda.synchronize()
+        launches = idx.kernel_launches() - launches0
         clocks = sampler.stop()
         ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+        # end to end: the host-buffer call (rv_index_rank_turboquant), host clock
+        e2e_t = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            idx.topk_turboquant(qh, top_k)
+            e2e_t.append(time.perf_counter() - t0)
+        e2e_s = sum(e2e_t) / len(e2e_t)
         # passes over the codes: the scan shares each code word among up to 8 queries (then 4, 2, 1
         # for the rest), as scan_qb in turbo_quant.cu
         passes, left = 0, nq
@@ -792,11 +906,20 @@ def run_turboquant(args):
                 "data": "synthetic normalised Gaussian rows",
                 "config": {"workload": "rank_turboquant", "rows": n_rows, "dim": dim, "queries": nq, "top_k": top_k,
                            "bits": 4, "l2": "codes (19.2 GB) larger than L2, no flush"},
-                "build_s": build_s, "clocks": clocks,
+                "build_s": build_s, "clocks": clocks, "gpu_launches": launches,
+                "e2e": {"value": nq / e2e_s, "unit": "queries/s", "h2d_bytes_per_step": nq * dim * 4,
+                        "d2h_bytes_per_step": nq * top_k * 12 + nq * 4,
+                        "how": "rv_index_rank_turboquant with host queries and results, host clock"},
                 "roofline": {"kernel": "rank_turboquant step (code scan + selection + exact rescoring)",
                              "bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
                              "frac": ach / pk["hbm_gbs"], "peak_source": f"{pk['source']} hbm_gbs",
                              "traffic": None, "bytes_per_step": code_bytes}}
+        lines.append(line)
+    # the CPU sample after every GPU measurement
+    cpu_base = None if args.no_cpu_baseline else cpu_turboquant_baseline(n_rows, dim, top_k)
+    for line in lines:
+        if cpu_base is not None:
+            line["cpu_baseline"] = cpu_base
         print(json.dumps(line), flush=True)
     idx.close()
 
@@ -828,10 +951,12 @@ def run_duplicates(args):
     sampler = ClockSampler(physical_gpu(local))
     sampler.start()
     times = []
+    launches0 = idx.kernel_launches()
     for _ in range(args.steps):
         t0 = time.perf_counter()
         a, b, s, s64 = idx.duplicate_pairs(0.85, 20)  # synchronous: host results at return
         times.append(time.perf_counter() - t0)
+    launches = idx.kernel_launches() - launches0
     clocks = sampler.stop()
     sec = sum(times) / len(times)
     flops = float(n) * (n - 1) / 2 * 2 * dim
@@ -843,11 +968,16 @@ def run_duplicates(args):
             "data": "synthetic normalised Gaussian rows with 64 planted near-copies",
             "config": {"workload": "find_duplicates", "rows": n, "dim": dim, "threshold": 0.85, "max_pairs": 20,
                        "timing": "host clock around the synchronous call (results on the host)"},
-            "pairs_found": int(len(a)), "clocks": clocks,
+            "pairs_found": int(len(a)), "clocks": clocks, "gpu_launches": launches,
+            "e2e": {"value": n * (n - 1) / 2 / sec, "unit": "pairs/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": int(len(a)) * 28,
+                    "how": "the timed call itself: rv_index_find_duplicates returns host arrays"},
             "roofline": {"kernel": "find_duplicates (tcgen05 strip GEMMs + pair filter + exact rescoring)",
                          "bound": "tensor", "achieved": ach, "peak": pk["bf16_sus"], "unit": "TFLOP/s",
                          "frac": ach / pk["bf16_sus"], "peak_source": f"{pk['source']} bf16_tflops_sustained",
                          "traffic": None, "flops_per_step": flops}}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_duplicates_baseline(dim)
     print(json.dumps(line), flush=True)
     idx.close()
 
@@ -966,6 +1096,7 @@ def run_cascade(args):
     build_s = time.perf_counter() - t0
     del db
     pk = peaks()
+    lines = []
     for nq in [int(v) for v in str(args.queries).split(",")]:
         q = synth.normalized_gaussian(nq, dim, seed=99)
         for _ in range(args.warmup):
@@ -974,10 +1105,12 @@ def run_cascade(args):
         sampler = ClockSampler(physical_gpu(local))
         sampler.start()
         times = []
+        launches0 = idx.kernel_launches()
         for _ in range(args.steps):
             t1 = time.perf_counter()
             idx.topk_cascade(q, top_k)
             times.append(time.perf_counter() - t1)
+        launches = idx.kernel_launches() - launches0
         clocks = sampler.stop()
         sec = sum(times) / len(times)
         trunc_bytes = n_rows * t_dim * 2
@@ -989,11 +1122,19 @@ def run_cascade(args):
                 "config": {"workload": "rank_cascade", "rows": n_rows, "dim": dim, "truncated_dim": t_dim,
                            "queries": nq, "top_k": top_k,
                            "timing": "host clock around the synchronous call (host queries and results)"},
-                "build_s": build_s, "clocks": clocks,
+                "build_s": build_s, "clocks": clocks, "gpu_launches": launches,
+                "e2e": {"value": nq / sec, "unit": "queries/s", "h2d_bytes_per_step": nq * dim * 4,
+                        "d2h_bytes_per_step": nq * top_k * 12 + nq * 4,
+                        "how": "the timed call itself: rv_index_rank_cascade with host queries and results"},
                 "roofline": {"kernel": "rank_cascade step (exact scan of the truncated rows + full re-rank)",
                              "bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
                              "frac": ach / pk["hbm_gbs"], "peak_source": f"{pk['source']} hbm_gbs",
                              "traffic": None, "bytes_per_step": trunc_bytes}}
+        lines.append(line)
+    cpu_base = None if args.no_cpu_baseline else cpu_cascade_baseline(n_rows, dim, t_dim, top_k)
+    for line in lines:
+        if cpu_base is not None:
+            line["cpu_baseline"] = cpu_base
         print(json.dumps(line), flush=True)
     idx.close()
 

@@ -154,6 +154,8 @@ int rv_index_create(int device, const void* src, int64_t n, int32_t dim, int32_t
 void rv_index_destroy(rv_index* idx);
 const char* rv_index_last_error(const rv_index* idx);
 int64_t rv_index_size(const rv_index* idx);
+/* Kernels this index has launched so far (all search entry points; for benchmarks). */
+int64_t rv_index_kernel_launches(rv_index* idx);
 /* Global row index of this shard's first row (rows are numbered base + local row in results). */
 int rv_index_set_base(rv_index* idx, int64_t base);
 

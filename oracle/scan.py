@@ -158,6 +158,13 @@ def rank_cascade(rows: np.ndarray, query, top_k: int, threshold: float, cascade_
         return ei[0, :ec[0]], es[0, :ec[0]]
     rb = ops.to_bf16(rows)
     tr = ops.to_bf16(ln_truncate(rb, cascade_dim))
+    return rank_cascade_prepared(rb, tr, q[0], top_k, threshold, cascade_dim)
+
+
+def rank_cascade_prepared(rb: np.ndarray, tr: np.ndarray, query, top_k: int, threshold: float, cascade_dim: int):
+    """``rank_cascade``'s query work on an index already built: ``rb`` the bf16 rows (as f32),
+    ``tr`` their bf16 truncated LayerNorm rows (``ln_truncate``)."""
+    q = np.asarray(query, np.float32).reshape(1, -1)
     tq = ln_truncate(q, cascade_dim)
     pre = max(100, 3 * top_k)
     ci, _, cc = topk_exact(tr, tq, pre)
@@ -198,6 +205,45 @@ def find_duplicates(rows: np.ndarray, threshold: float, max_pairs: int):
     a, b, sc = np.concatenate(aa), np.concatenate(bb), np.concatenate(ss)
     order = np.lexsort((b, a, -sc))[:max_pairs]
     return a[order].astype(np.int64), b[order].astype(np.int64), sc[order]
+
+
+def rank_cascade_f32(rows: np.ndarray, tr: np.ndarray, query, top_k: int, threshold: float, cascade_dim: int):
+    """The reference's own arithmetic for ``rank_cascade`` (``index.rs:245-297``) on a built index
+    (``tr`` = ``ln_truncate(rows, cascade_dim)``): the truncated query, an f32 GEMV over ``tr``, a
+    full sort of the scores, the first ``max(100, 3 top_k)``, full-dimension f32 dot products for
+    those, threshold, sort, ``top_k``.  Used as the timed CPU baseline; parity uses
+    ``rank_cascade``."""
+    q = np.asarray(query, np.float32).reshape(1, -1)
+    tq = ln_truncate(q, cascade_dim)[0]
+    s = np.asarray(tr, np.float32) @ tq
+    cand = np.argsort(-s, kind="stable")[:max(100, 3 * top_k)]
+    full = np.asarray(rows, np.float32)[cand] @ q[0]
+    keep = full >= np.float32(threshold)
+    cand, full = cand[keep], full[keep]
+    order = np.argsort(-full, kind="stable")[:top_k]
+    return cand[order], full[order]
+
+
+def find_duplicates_f32(rows: np.ndarray, threshold: float, max_pairs: int, block: int = 4096):
+    """The reference's own arithmetic for ``find_duplicates`` (``index.rs:325-348``): the f32
+    similarity matrix E Eᵀ by BLAS (here in row blocks of the upper triangle), pairs a < b with
+    score >= threshold, sorted by descending score, the first ``max_pairs``.  Ties are left as
+    the sort leaves them (the reference uses ``sort_unstable_by``).  Used as the timed CPU
+    baseline; parity uses ``find_duplicates``."""
+    e = np.ascontiguousarray(rows, np.float32)
+    n = e.shape[0]
+    aa, bb, ss = [], [], []
+    for r0 in range(0, n, block):
+        r1 = min(n, r0 + block)
+        s = e[r0:r1] @ e[r0:].T
+        i, j = np.nonzero(s >= np.float32(threshold))
+        up = j > i
+        aa.append(i[up] + r0)
+        bb.append(j[up] + r0)
+        ss.append(s[i[up], j[up]])
+    a, b, sc = np.concatenate(aa), np.concatenate(bb), np.concatenate(ss)
+    order = np.argsort(-sc, kind="stable")[:max_pairs]
+    return a[order], b[order], sc[order]
 
 
 def merge_topk(idx_lists: np.ndarray, score_lists: np.ndarray, k: int, threshold: float = -np.inf):

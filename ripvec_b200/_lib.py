@@ -88,6 +88,7 @@ SIGNATURES = {
     "rv_index_destroy": (None, [vp]),
     "rv_index_last_error": (C.c_char_p, [vp]),
     "rv_index_size": (i64, [vp]),
+    "rv_index_kernel_launches": (i64, [vp]),
     "rv_index_set_base": (C.c_int, [vp, i64]),
     "rv_index_topk": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),
     "rv_index_topk_device": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp, vp]),

@@ -385,24 +385,35 @@ int finalize_classic(rv_ctx* c) {
     if ((rc = need(c, p + "attention.self.query.weight", &q))) return rc;
     if ((rc = need(c, p + "attention.self.key.weight", &k))) return rc;
     if ((rc = need(c, p + "attention.self.value.weight", &v))) return rc;
-    std::vector<float> qkv;  // rows Q, K, V concatenated (backend/cpu.rs:526-533)
-    qkv.reserve(q->size() * 3);
-    qkv.insert(qkv.end(), q->begin(), q->end());
-    qkv.insert(qkv.end(), k->begin(), k->end());
-    qkv.insert(qkv.end(), v->begin(), v->end());
-    if ((rc = up_matrix(c, qkv, 3 * H, H, 128, &lw.wqkv))) return rc;
+    // Rows Q, K, V concatenated (backend/cpu.rs:526-533); with a padded attention width, head h's
+    // hd rows of each go to rows h * 64 .. h * 64 + hd - 1 of its block and the rest are zero.
+    const int W = c->attn_width, heads = c->d.num_heads, hd = H / heads, hs = W / heads;
+    std::vector<float> qkv(size_t(3) * W * H, 0.0f);
+    const std::vector<float>* parts[3] = {q, k, v};
+    for (int m = 0; m < 3; ++m)
+      for (int r = 0; r < H; ++r)
+        std::copy(parts[m]->begin() + size_t(r) * H, parts[m]->begin() + size_t(r + 1) * H,
+                  qkv.begin() + (size_t(m) * W + size_t(r / hd) * hs + r % hd) * H);
+    if ((rc = up_matrix(c, qkv, 3 * W, H, 128, &lw.wqkv))) return rc;
     const std::vector<float>*qb = get_w(c, p + "attention.self.query.bias"),
                       *kb = get_w(c, p + "attention.self.key.bias"),
                       *vb = get_w(c, p + "attention.self.value.bias");
     if (qb && kb && vb) {
-      std::vector<float> b;
-      b.insert(b.end(), qb->begin(), qb->end());
-      b.insert(b.end(), kb->begin(), kb->end());
-      b.insert(b.end(), vb->begin(), vb->end());
+      std::vector<float> b(size_t(3) * W, 0.0f);
+      const std::vector<float>* bs[3] = {qb, kb, vb};
+      for (int m = 0; m < 3; ++m)
+        for (int r = 0; r < H; ++r) b[size_t(m) * W + size_t(r / hd) * hs + r % hd] = (*bs[m])[r];
       if ((rc = up_f32(c, b, &lw.bqkv))) return rc;
     }
     if ((rc = need(c, p + "attention.output.dense.weight", &w))) return rc;
-    if ((rc = up_matrix(c, *w, H, H, 128, &lw.wo))) return rc;
+    if (W == H) {
+      if ((rc = up_matrix(c, *w, H, H, 128, &lw.wo))) return rc;
+    } else {  // context columns padded like Q, K, V: zero weights for the pad columns
+      std::vector<float> wo(size_t(H) * W, 0.0f);
+      for (int r = 0; r < H; ++r)
+        for (int col = 0; col < H; ++col) wo[size_t(r) * W + size_t(col / hd) * hs + col % hd] = (*w)[size_t(r) * H + col];
+      if ((rc = up_matrix(c, wo, H, W, 128, &lw.wo))) return rc;
+    }
     if ((rc = opt_f32(p + "attention.output.dense.bias", &lw.bo))) return rc;
     if ((rc = need(c, p + "attention.output.LayerNorm.weight", &w))) return rc;
     if ((rc = up_f32(c, *w, &lw.ln1_w))) return rc;
@@ -428,8 +439,9 @@ int alloc_workspaces(rv_ctx* c) {
   const size_t es = 2;
   c->x = dalloc(c, size_t(T) * H * es);
   c->hn = dalloc(c, size_t(T) * H * es);
-  c->qkv = dalloc(c, size_t(T) * 3 * H * es);
-  c->cbuf = dalloc(c, size_t(T) * H * es);
+  const int W = c->attn_width;
+  c->qkv = dalloc(c, size_t(T) * 3 * W * es);
+  c->cbuf = dalloc(c, size_t(T) * W * es);
   c->act = dalloc(c, size_t(T) * I * es);
   if (is_modern(c) && c->ln_fused) {
     c->stats_a = dalloc(c, size_t(T) * 4 * sizeof(float2));
@@ -457,7 +469,8 @@ int alloc_workspaces(rv_ctx* c) {
   const bool bf = c->adt == Act::kBf16;
   if (!rv::make_tmap_2d_16bit(&c->map_x, c->x, bf, H, T, uint64_t(H) * 2, 64, 128, &why) ||
       !rv::make_tmap_2d_16bit(&c->map_hn, c->hn, bf, H, T, uint64_t(H) * 2, 64, 128, &why) ||
-      !rv::make_tmap_2d_16bit(&c->map_c, c->cbuf, bf, H, T, uint64_t(H) * 2, 64, 128, &why) ||
+      !rv::make_tmap_2d_16bit(&c->map_c, c->cbuf, bf, c->attn_width, T, uint64_t(c->attn_width) * 2, 64, 128,
+                              &why) ||
       !rv::make_tmap_2d_16bit(&c->map_act, c->act, bf, I, T, uint64_t(I) * 2, 64, 128, &why) ||
       !rv::make_tmap_2d_16bit(&c->map_qkv_out, c->qkv, bf, 3 * H, T, uint64_t(3 * H) * 2, 64, 128, &why) ||
       !rv::make_tmap_2d_16bit(&c->map_act_out, c->act, bf, I, T, uint64_t(I) * 2, 32, 128, &why, 64))
@@ -509,7 +522,7 @@ int forward(rv_ctx* c, const int* ids, int T, int n, int total_q_tiles, int tota
   RV_LAUNCH_K(c, RV_KIND_EMBED, 0, rv::build_positions(cu, n, T, c->pos_d, st));
   const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
   auto attend = [&](int window_half) {
-    return c->attn_tc && hd == 64
+    return c->attn_tc && (hd == 64 || c->attn_width == 64 * heads)
                ? rv::attention_varlen_tc(c->adt, c->qkv, c->cbuf, T, c->tiles_d, total_q_tiles128, heads,
                                          window_half, scale, c->d_err, st)
                : rv::attention_varlen(c->adt, c->qkv, c->cbuf, cu, qts, n, total_q_tiles, heads, hd,
@@ -572,7 +585,7 @@ int forward(rv_ctx* c, const int* ids, int T, int n, int total_q_tiles, int tota
     for (int l = 0; l < c->d.num_layers; ++l) {
       const rv::LayerWeights& lw = c->layers[l];
       int rc;
-      if ((rc = gemm(c, c->map_x, lw.wqkv, T, GemmEpi::kBias, c->qkv, 3 * H, lw.bqkv))) return rc;
+      if ((rc = gemm(c, c->map_x, lw.wqkv, T, GemmEpi::kBias, c->qkv, 3 * c->attn_width, lw.bqkv))) return rc;
       RV_LAUNCH_K(c, RV_KIND_ATTENTION, 4.0 * H * pairs_global,
                   attend(-1));
       if ((rc = gemm(c, c->map_c, lw.wo, T, GemmEpi::kResidual, c->x, H, lw.bo))) return rc;
@@ -791,6 +804,16 @@ int rv_create(const rv_model_desc* desc, int device, rv_ctx** out) {
   c->n_max = 65536;
   // The tcgen05 attention addresses the context with 32-bit element offsets.
   if (c->t_max * int64_t(d.hidden) > INT32_MAX) c->attn_tc = false;
+  // head_dim 32: Q, K, V and the context are laid out with 64 columns per head (32 zeros), so the
+  // tcgen05 head_dim-64 kernel computes the same scores and context.
+  c->attn_width = d.hidden;
+  if (c->attn_tc && d.num_heads > 0 && d.hidden == 32 * d.num_heads) {
+    c->attn_width = 64 * d.num_heads;
+    if (c->t_max * int64_t(c->attn_width) > INT32_MAX) {
+      c->attn_tc = false;
+      c->attn_width = d.hidden;
+    }
+  }
   if (cudaSetDevice(device) != cudaSuccess) return RV_E_CUDA;
   if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return RV_E_CUDA;
   c->d_err = static_cast<unsigned int*>(dalloc(c.get(), 4));

@@ -117,7 +117,10 @@ struct rv_ctx {
   CUtensorMap map_x, map_hn, map_c, map_act;
   CUtensorMap map_qkv_out, map_act_out;  // TMA-staged epilogue outputs (x uses map_x)
   bool tma_epi = true;                   // TMA-staged GEMM epilogues (RV_TMA_EPI=0 turns off)
-  bool attn_tc = true;                   // tcgen05 attention for head_dim 64 (RV_ATTN_TC=0 turns off)
+  bool attn_tc = true;                   // tcgen05 attention (RV_ATTN_TC=0 turns off)
+  // Columns of each of Q, K, V in qkv and of the attention context cbuf: hidden, or heads x 64
+  // when head_dim 32 (BERT-small) is zero-padded to 64 per head for the tcgen05 attention.
+  int attn_width = 0;
 
   std::vector<void*> allocations;
 

@@ -409,6 +409,11 @@ void rv_index_destroy(rv_index* x) {
 
 const char* rv_index_last_error(const rv_index* x) { return x ? x->err.c_str() : "null index"; }
 int64_t rv_index_size(const rv_index* x) { return x ? x->n : 0; }
+int64_t rv_index_kernel_launches(rv_index* x) {
+  if (!x) return 0;
+  std::lock_guard<std::mutex> lk(x->mu);
+  return x->launches;
+}
 int rv_index_set_base(rv_index* x, int64_t base) {
   if (!x || base < 0) return RV_E_INVALID;
   std::lock_guard<std::mutex> lk(x->mu);

@@ -91,6 +91,10 @@ class SearchIndex:
     def __len__(self) -> int:
         return int(self._lib.rv_index_size(self._h))
 
+    def kernel_launches(self) -> int:
+        """Kernels launched by this index so far."""
+        return int(self._lib.rv_index_kernel_launches(self._h))
+
     def export_rows(self, row0: int = 0, n: int | None = None, bf16_bits: bool = False) -> np.ndarray:
         """Rows ``[row0, row0 + n)`` as stored on the device (``rv_index_export``): widened to f32
         (exact), or with ``bf16_bits`` the raw bf16 values as uint16."""
@@ -113,6 +117,10 @@ class SearchIndex:
 
     def __len__(self) -> int:
         return int(self._lib.rv_index_size(self._h))
+
+    def kernel_launches(self) -> int:
+        """Kernels launched by this index so far."""
+        return int(self._lib.rv_index_kernel_launches(self._h))
 
     def is_empty(self) -> bool:
         return len(self) == 0
