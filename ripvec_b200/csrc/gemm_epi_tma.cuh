@@ -79,6 +79,21 @@ struct TEpiResidualStats {
   }
 };
 
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// Folded LayerNorm of four values, two per instruction: rstd * (v - mu * c) evaluated as
+// v * rstd + (-rstd * mu) * c (r2 = {rstd, rstd}, nm2 = {-rstd * mu, -rstd * mu}).
+__device__ __forceinline__ void ln_fold4(float* v, const float4 c, uint64_t r2, uint64_t nm2) {
+  uint64_t a = f2_fma(f2_pack(v[0], v[1]), r2, f2_mul(nm2, f2_pack(c.x, c.y)));
+  uint64_t b = f2_fma(f2_pack(v[2], v[3]), r2, f2_mul(nm2, f2_pack(c.z, c.w)));
+  f2_unpack(a, v[0], v[1]);
+  f2_unpack(b, v[2], v[3]);
+}
+
 // Rotary embedding of the Q / K heads (columns < rope_cols), optionally after a folded LayerNorm.
 template <typename T, bool kNorm>
 struct TEpiQkv {
@@ -117,27 +132,30 @@ struct TEpiQkv {
                                           float (&v1)[32], bool) const {
     if (kNorm) {
       const float4* cs = reinterpret_cast<const float4*>(cs_smem + col);
+      const float nm = -t.rstd * t.mu;
+      const uint64_t r2 = f2_pack(t.rstd, t.rstd), nm2 = f2_pack(nm, nm);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float4 c0 = cs[i], c1 = cs[8 + i];
-        const float ca[4] = {c0.x, c0.y, c0.z, c0.w}, cb[4] = {c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          v0[4 * i + j] = t.rstd * (v0[4 * i + j] - t.mu * ca[j]);
-          v1[4 * i + j] = t.rstd * (v1[4 * i + j] - t.mu * cb[j]);
-        }
+        ln_fold4(&v0[4 * i], cs[i], r2, nm2);
+        ln_fold4(&v1[4 * i], cs[8 + i], r2, nm2);
       }
     }
     if (col < rope_cols) {
+      // (f, s) -> (f cc - s ss, f ss + s cc), two columns per instruction.
+      const uint64_t m1 = f2_pack(-1.f, -1.f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float cc[4] = {t.cv[i].x, t.cv[i].y, t.cv[i].z, t.cv[i].w};
-        const float ss[4] = {t.sv[i].x, t.sv[i].y, t.sv[i].z, t.sv[i].w};
+        const float4 c = t.cv[i], n = t.sv[i];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float f = v0[4 * i + j], s = v1[4 * i + j];
-          v0[4 * i + j] = f * cc[j] - s * ss[j];
-          v1[4 * i + j] = f * ss[j] + s * cc[j];
+        for (int h = 0; h < 2; ++h) {
+          const uint64_t cc = h ? f2_pack(c.z, c.w) : f2_pack(c.x, c.y);
+          const uint64_t ss = h ? f2_pack(n.z, n.w) : f2_pack(n.x, n.y);
+          const uint64_t f = f2_pack(v0[4 * i + 2 * h], v0[4 * i + 2 * h + 1]);
+          const uint64_t s = f2_pack(v1[4 * i + 2 * h], v1[4 * i + 2 * h + 1]);
+          const uint64_t o0 = f2_fma(f2_mul(s, ss), m1, f2_mul(f, cc));
+          const uint64_t o1 = f2_fma(f, ss, f2_mul(s, cc));
+          f2_unpack(o0, v0[4 * i + 2 * h], v0[4 * i + 2 * h + 1]);
+          f2_unpack(o1, v1[4 * i + 2 * h], v1[4 * i + 2 * h + 1]);
         }
       }
     }
@@ -165,16 +183,14 @@ struct TEpiNormGeglu {
   __device__ __forceinline__ void compute(Tile& t, int, int col, const float*, float (&v0)[32],
                                           float (&v1)[32], bool) const {
     const float4* cs = reinterpret_cast<const float4*>(cs_smem + col);
+    const float nm = -t.rstd * t.mu;
+    const uint64_t r2 = f2_pack(t.rstd, t.rstd), nm2 = f2_pack(nm, nm);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float4 c0 = cs[i], c1 = cs[8 + i];
-      const float ca[4] = {c0.x, c0.y, c0.z, c0.w}, cb[4] = {c1.x, c1.y, c1.z, c1.w};
+      ln_fold4(&v0[4 * i], cs[i], r2, nm2);
+      ln_fold4(&v1[4 * i], cs[8 + i], r2, nm2);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float a = t.rstd * (v0[4 * i + j] - t.mu * ca[j]);
-        const float g = t.rstd * (v1[4 * i + j] - t.mu * cb[j]);
-        v0[4 * i + j] = gelu_tanh_fast(a) * g;
-      }
+      for (int j = 0; j < 4; ++j) v0[4 * i + j] = gelu_tanh_fast(v0[4 * i + j]) * v1[4 * i + j];
     }
   }
 };
