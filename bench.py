@@ -22,6 +22,11 @@ every rank embeds its own 4096 chunks).
 * ``parity``: min / p50 cosine of 16 chunks of the timed output against that port.
 * ``sweep_tokens_per_s`` (config 4, strong scaling): 100k log-normal chunks sharded over the
   ranks by token count, max over ranks of the device time.
+* ``long_tokens_per_s`` (config 3, weak scaling): ModernBERT-base in fp16 over 512 chunks of
+  U[2048, 8192] tokens per rank, max over ranks; on one GPU with the longest chunk's cosine
+  against the fp32 port.
+* ``classic_tokens_per_s`` (config 1, weak scaling): BERT-small ClassicBert over 64 chunks of
+  U[32, 256] tokens per rank, with all 64 chunks' cosine against the fp32 port on rank 0.
 * ``scan_step_ms`` (config 5): one 1024-query top-100 step over a 10M x 768 bf16 database
   row-sharded over the ranks, through ``rv_index_topk_sharded`` (the library's NCCL all-gather
   of the per-shard lists and device merge).
@@ -77,7 +82,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the 16-chunk oracle check of the timed output")
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip the sweep (config 4) and sharded-scan (config 5) keys of the encoder line")
+                    help="skip the config 1, 3, 4 and 5 keys of the encoder line (classic, long, sweep, scan)")
     ap.add_argument("--sweep-chunks", type=int, default=100_000,
                     help="chunks of the strong-scaling sweep key (log-normal lengths, all ranks together)")
     return ap.parse_args()
@@ -459,6 +464,91 @@ def sweep_extra(args, torch, be, spec, barrier, max_over_ranks, rank, world, str
             "rank0_chunks": int(len(lengths)), "rank0_tokens": int(cu[-1])}
 
 
+def timed_device_passes(torch, be, ids_dev, cu, out, stream, steps, flush):
+    """Device time (ms) of ``steps`` encoder passes over one packed set with the ids in HBM, CUDA
+    events on the launching stream, L2 flushed before each pass (outside the events)."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for s in range(steps):
+        flush.zero_()
+        evs[s][0].record(stream)
+        be.embed_device(ids_dev, cu, out, stream=stream.cuda_stream)
+        evs[s][1].record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs)
+
+
+def long_extra(args, torch, local, barrier, max_over_ranks, rank, world, stream, flush):
+    """Config 3 as a key of the encoder line: ModernBERT-base in fp16 over 512 chunks of U[2048, 8192]
+    tokens per rank (weak scaling, the ``--workload long`` set), one warm-up pass and two timed
+    passes with the ids in HBM, max over ranks.  On one GPU the longest chunk of the set (RoPE
+    positions up to about 8192) is checked against the fp32 oracle at the fp16 bar; that check
+    costs about a minute of host time, so the multi-GPU runs leave it to the tests."""
+    from ripvec_b200 import MODERNBERT_BASE, EmbedBackend, synth
+
+    n = 512
+    lengths = synth.uniform_lengths(n, 2048, 8192, seed=2000 + rank)
+    ids, cu = synth.packed_ids(lengths, MODERNBERT_BASE.vocab, seed=3000 + rank)
+    w = synth.random_weights(MODERNBERT_BASE, seed=1)
+    be = EmbedBackend(MODERNBERT_BASE, w, dtype="f16", device=local, max_batch_tokens=args.max_batch_tokens)
+    ids_dev = torch.from_numpy(ids).cuda()
+    out = torch.empty(n, MODERNBERT_BASE.hidden, device="cuda", dtype=torch.float32)
+    be.embed_device(ids_dev, cu, out, stream=stream.cuda_stream)
+    barrier()
+    steps = 2
+    ms = max_over_ranks(timed_device_passes(torch, be, ids_dev, cu, out, stream, steps, flush) / steps)
+    barrier()
+    res = {"tokens_per_s": int(cu[-1]) * world / (ms / 1e3), "ms_per_step": ms, "chunks_per_gpu": n,
+           "tokens_per_gpu": int(cu[-1]), "lengths": "U[2048,8192]", "dtype": "f16", "steps": steps, "warmup": 1,
+           "scaling": "weak", "l2": "flushed between passes"}
+    if rank == 0 and world == 1 and not args.no_parity:
+        b = int(np.argmax(lengths))
+        pin_blas_threads()
+        ref = cpu_embed_one(MODERNBERT_BASE, w, ids[cu[b]:cu[b + 1]])
+        g = out[b].double().cpu().numpy()
+        cos = float(g @ ref / max(np.linalg.norm(g) * np.linalg.norm(ref), 1e-300))
+        res["parity"] = {"min_cos": cos, "bar": 0.9999, "chunks": 1, "sample_lengths": [int(lengths[b])],
+                         "against": "numpy fp32 port of the reference CPU path, the longest chunk of the set"}
+        if cos < 0.9999:
+            raise RuntimeError(f"config-3 parity below the fp16 bar: {res['parity']}")
+    be.close()
+    return res
+
+
+def classic_extra(args, torch, local, barrier, max_over_ranks, rank, world, stream, flush):
+    """Config 1 as a key of the encoder line: BERT-small ClassicBert (f16 storage, mean pooling)
+    over the 64 chunks of U[32, 256] tokens on every rank (weak scaling), five timed passes with
+    the ids in HBM, max over ranks; rank 0 checks all 64 chunks against the fp32 oracle (bar
+    0.9999)."""
+    from ripvec_b200 import EmbedBackend
+
+    spec, w, lengths, ids, cu = classic_workload()
+    n = len(lengths)
+    be = EmbedBackend(spec, w, dtype="f16", device=local, pooling="mean")
+    ids_dev = torch.from_numpy(ids).cuda()
+    out = torch.empty(n, spec.hidden, device="cuda", dtype=torch.float32)
+    for _ in range(3):
+        be.embed_device(ids_dev, cu, out, stream=stream.cuda_stream)
+    barrier()
+    steps = 5
+    ms = max_over_ranks(timed_device_passes(torch, be, ids_dev, cu, out, stream, steps, flush) / steps)
+    barrier()
+    res = {"tokens_per_s": int(cu[-1]) * world / (ms / 1e3), "ms_per_step": ms, "chunks_per_gpu": n,
+           "tokens_per_gpu": int(cu[-1]), "lengths": "U[32,256]", "dtype": "f16", "pooling": "mean",
+           "steps": steps, "warmup": 3, "scaling": "weak", "l2": "flushed between passes"}
+    if rank == 0 and not args.no_parity:
+        pin_blas_threads()
+        ref, _ = classic_oracle(spec, w, ids, cu)
+        a = out.double().cpu().numpy()
+        b = ref.astype(np.float64)
+        cos = (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+        res["parity"] = {"min_cos": float(cos.min()), "p50_cos": float(np.median(cos)), "bar": 0.9999, "chunks": n,
+                         "against": "numpy fp32 port of the reference CPU path, all 64 chunks"}
+        if cos.min() < 0.9999:
+            raise RuntimeError(f"config-1 parity below the bar: {res['parity']}")
+    be.close()
+    return res
+
+
 def scan_extra(args, torch, dist, rank, world, local, barrier, max_over_ranks, stream):
     """Config 5 as a key of the encoder line: one 1024-query top-100 step over a 10M x 768 bf16
     database row-sharded across the ranks, through rv_index_topk_sharded (shard top-k, one NCCL
@@ -647,9 +737,13 @@ def run_encoder(args):
         cpu = {"value": r, "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"first {nc} chunks of the workload ({tok} tokens, {dt:.1f} s), numpy fp32 port of the reference CPU path"}
 
-    sweep = scan = None
+    sweep = scan = long_ = classic = None
     if args.workload == "encoder" and not args.no_extras:
         sweep = sweep_extra(args, torch, be, spec, barrier, max_over_ranks, rank, world, stream)
+        be.close()
+        del ids_dev, out_dev
+        long_ = long_extra(args, torch, local, barrier, max_over_ranks, rank, world, stream, flush)
+        classic = classic_extra(args, torch, local, barrier, max_over_ranks, rank, world, stream, flush)
         scan = scan_extra(args, torch, dist, rank, world, local, barrier, max_over_ranks, stream)
 
     if dist is not None:
@@ -670,6 +764,12 @@ def run_encoder(args):
         if sweep is not None:
             line["sweep_tokens_per_s"] = sweep["tokens_per_s"]
             line["sweep"] = sweep
+        if long_ is not None:
+            line["long_tokens_per_s"] = long_["tokens_per_s"]
+            line["long"] = long_
+        if classic is not None:
+            line["classic_tokens_per_s"] = classic["tokens_per_s"]
+            line["classic"] = classic
         if scan is not None:
             line["scan_step_ms"] = scan["step_ms"]
             line["scan"] = scan
