@@ -339,6 +339,12 @@ int rv_op_attention(int32_t act_dtype, const void* qkv, void* ctx_out, const int
  * Nothing faults, traps or spins without bound.  enable = 0 restores normal launches.  Process
  * wide; for tests only. */
 int rv_debug_stall_attention(int32_t enable, int64_t wait_limit_cycles);
+/* Test hook (no counterpart in the reference): y[i] = 2^x[i] by the tcgen05 attention's
+ * FMA-pipe exponential (range reduction by rint, degree-3 minimax polynomial, exponent add;
+ * relative error below 7.6e-5 for x in [-125, 126], 0 below -125), which its
+ * softmax computes for a quarter of the fully visible exponentials beside the MUFU ex2 when the
+ * environment sets RV_ATTN_EXP2_POLY=1.  Device pointers; synchronous on stream. */
+int rv_debug_exp2_poly(const float* x, float* y, int64_t n, void* stream);
 /* out = LN(in) * gamma (+ beta); 16-bit rows. */
 int rv_op_layernorm(int32_t act_dtype, const void* in, void* out, int32_t rows, int32_t hidden,
                     const float* gamma, const float* beta, float eps, void* stream);

@@ -119,6 +119,7 @@ SIGNATURES = {
     "rv_op_gemm": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "rv_op_attention": (C.c_int, [i32, vp, vp, vp, i32, i32, i32, i32, f32, vp]),
     "rv_debug_stall_attention": (C.c_int, [i32, i64]),
+    "rv_debug_exp2_poly": (C.c_int, [vp, vp, i64, vp]),
     "rv_op_layernorm": (C.c_int, [i32, vp, vp, i32, i32, vp, vp, f32, vp]),
 }
 

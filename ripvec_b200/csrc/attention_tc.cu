@@ -20,7 +20,8 @@
 //   softmax             each thread reads its row's 64 scores with tcgen05.ld, masks keys past
 //                       the sequence end and, on sliding-window layers, keys with |i - j| > w/2
 //                       (32-key halves that no row of the warp can see skip the exponentials);
-//                       P = exp2(s - m) is
+//                       P = exp2(s - m) (MUFU ex2; with RV_ATTN_EXP2_POLY=1 one pair in
+//                       four on the FMA pipe by exp2_poly) is
 //                       written as packed 16-bit pairs over S[g%3] in TMEM (tcgen05.st),
 //   O += P V            tcgen05.mma M=128 N=64 K=64 with P (A) read from TMEM and V as an
 //                       MN-major shared-memory operand, into the TMEM accumulator O; the
@@ -33,6 +34,8 @@
 // masked keys get weight 0 exactly, as exp(-1e9 - max) does in f32.
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <vector>
 
 #include "common.cuh"
@@ -66,6 +69,31 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA and integer pipes instead of the MUFU unit, so that part of the softmax
+// exponentials can run beside the hardware ex2.  Method: Cody-Waite style range reduction
+// x = n + f with n = rint(x), taken from the round-to-nearest sum x + 1.5 * 2^23 (whose low
+// mantissa bits hold n), f = x - n exact in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose
+// coefficients are this project's own Remez (minimax relative error) fit on [-1/2, 1/2]; 2^n by
+// adding n to the exponent field.  Relative error below 7.6e-5 for x in [-125, 126] (the
+// polynomial's minimax error; the reduction and the scaling are exact), against 2^-9 and 2^-12
+// for the bf16 and f16 rounding of P.  Below -125 the result is 0, so a masked score (-inf)
+// gets weight 0 exactly, as with ex2.approx.ftz, which also flushes results below 2^-126.
+constexpr float kExpShift = 12582912.0f;  // 1.5 * 2^23
+constexpr float kExpC0 = 0.99992806f, kExpC1 = 0.69326097f, kExpC2 = 0.24261113f, kExpC3 = 0.055171669f;
+__device__ __forceinline__ float exp2_poly(float x) {
+  // Scalar arithmetic, so that the constants come from the constant bank rather than registers.
+  const float xc = fmaxf(x, -125.f);
+  const float t = __fadd_rn(xc, kExpShift);  // 1.5 * 2^23 + rint(x)
+  const float n = __fsub_rn(t, kExpShift);   // rint(x), exact
+  const float f = __fsub_rn(xc, n);          // x - rint(x), exact
+  float p = fmaf(kExpC3, f, kExpC2);
+  p = fmaf(p, f, kExpC1);
+  p = fmaf(p, f, kExpC0);
+  // t's bits are those of 1.5 * 2^23 plus n; shifted left by 23 only n << 23 remains (mod 2^32).
+  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+  return x < -125.f ? 0.f : r;
 }
 
 // Shared-memory descriptor of an MN-major operand tile written by TMA with 128-byte swizzling:
@@ -128,8 +156,9 @@ __device__ __forceinline__ float masked_max(float (&s)[32], int cls, int kb, int
 
 // P = exp2(s * scale_log2 - m) of 32 keys as 16 packed 16-bit pairs (zeros when the half is
 // not visible); adds the f32 values to the two packed partial sums ps.  sl2 = {scale_log2,
-// scale_log2}, nm2 = {-m, -m}.
-template <typename T>
+// scale_log2}, nm2 = {-m, -m}.  With kPoly, one pair in four is computed with exp2_poly on the
+// FMA pipe and the rest with the MUFU ex2, so the two units share the exponentials.
+template <typename T, bool kPoly>
 __device__ __forceinline__ void make_p(bool live, const float (&s)[32], uint64_t sl2, uint64_t nm2,
                                        uint64_t (&ps)[2], uint32_t (&w)[16]) {
   // One branch for the whole half (not one per pair), so the 32 exponentials form a single
@@ -141,14 +170,22 @@ __device__ __forceinline__ void make_p(bool live, const float (&s)[32], uint64_t
   }
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
-    // Masked scores are -inf: exp2(-inf) = 0 exactly.
+    // Masked scores are -inf: exp2(-inf) = 0 exactly (ex2 and exp2_poly alike).
     float x0, x1;
     f2_unpack(f2_fma(f2_pack(s[2 * e], s[2 * e + 1]), sl2, nm2), x0, x1);
-    const float p0 = ex2(x0), p1 = ex2(x1);
+    const bool fma_pipe = kPoly && (e & 3) == 3;
+    const float p0 = fma_pipe ? exp2_poly(x0) : ex2(x0);
+    const float p1 = fma_pipe ? exp2_poly(x1) : ex2(x1);
     ps[e & 1] = f2_add(ps[e & 1], f2_pack(p0, p1));
     auto v = Elem<T>::pack(p0, p1);
     w[e] = *reinterpret_cast<uint32_t*>(&v);
   }
+}
+
+// Evaluates exp2_poly on n floats (device pointers): the test hook that bounds its error.
+__global__ void exp2_poly_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    y[i] = exp2_poly(x[i]);
 }
 
 // The (item, key tile) sequence one CTA processes: items w = blockIdx.x + k * gridDim.x; item w
@@ -201,7 +238,7 @@ struct Walk {
   }
 };
 
-template <typename T>
+template <typename T, bool kPoly>
 __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_constant__ CUtensorMap tmQKV,
                                                               T* __restrict__ ctx,
                                                               const int2* __restrict__ tiles,
@@ -469,9 +506,9 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
         const uint64_t nm2 = f2_pack(-m, -m);
         uint64_t ps[2] = {0ull, 0ull};  // two packed partial sums (f32 zero bits)
         uint32_t w[16];
-        make_p<T>(cls0 != 0, s0, sl2, nm2, ps, w);
+        make_p<T, kPoly>(cls0 != 0, s0, sl2, nm2, ps, w);
         tmem_st16(trow + b * kBKV, w);
-        make_p<T>(cls1 != 0, s1, sl2, nm2, ps, w);
+        make_p<T, kPoly>(cls1 != 0, s1, sl2, nm2, ps, w);
         tmem_st16(trow + b * kBKV + 16, w);
         float p0, p1, p2, p3;
         f2_unpack(ps[0], p0, p1);
@@ -543,14 +580,14 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const __grid_const
 std::atomic<int> g_stall{0};
 std::atomic<long long> g_stall_limit{kWaitLimitCycles};
 
-template <typename T>
+template <typename T, bool kPoly>
 cudaError_t launch_attn_tc(const CUtensorMap& tm, void* ctx, const int2* tiles, int n_tiles,
                            int num_heads, int window_half, float scale, unsigned int* err,
                            cudaStream_t st) {
   static PerDeviceOnce attr_set;  // per-device attribute, set once under a lock
   {
     const cudaError_t e_once = attr_set.run([&]() -> cudaError_t {
-      cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>,
+      cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T, kPoly>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
       if (e != cudaSuccess) return e;
       return cudaSuccess;
@@ -563,9 +600,17 @@ cudaError_t launch_attn_tc(const CUtensorMap& tm, void* ctx, const int2* tiles, 
   const float scale_log2 = scale * 1.4426950408889634f;
   const int stall = g_stall.load(std::memory_order_relaxed);
   const long long limit = stall ? g_stall_limit.load(std::memory_order_relaxed) : kWaitLimitCycles;
-  attn_tc_kernel<T><<<grid, kThreads, kSmem, st>>>(tm, static_cast<T*>(ctx), tiles, n_tiles, n_items,
-                                                   num_heads * kD, window_half, scale_log2, err, limit, stall);
+  attn_tc_kernel<T, kPoly><<<grid, kThreads, kSmem, st>>>(tm, static_cast<T*>(ctx), tiles, n_tiles, n_items,
+                                                          num_heads * kD, window_half, scale_log2, err, limit,
+                                                          stall);
   return cudaGetLastError();
+}
+
+// Whether the softmax shares its exponentials between the MUFU ex2 and exp2_poly (environment
+// RV_ATTN_EXP2_POLY=1), read at every launch.
+bool use_exp2_poly() {
+  const char* e = std::getenv("RV_ATTN_EXP2_POLY");
+  return e && std::strcmp(e, "1") == 0;
 }
 
 }  // namespace
@@ -584,9 +629,19 @@ cudaError_t attention_varlen_tc(Act act, const void* qkv, void* ctx, int total_t
   if (!make_tmap_2d_16bit(&tm, qkv, act == Act::kBf16, uint64_t(3) * H, uint64_t(total_tokens),
                           uint64_t(3) * H * 2, 64, 64, nullptr))
     return cudaErrorInvalidValue;
+  const bool poly = use_exp2_poly();
   if (act == Act::kBf16)
-    return launch_attn_tc<__nv_bfloat16>(tm, ctx, tiles, n_tiles, num_heads, window_half, scale, err, st);
-  return launch_attn_tc<__half>(tm, ctx, tiles, n_tiles, num_heads, window_half, scale, err, st);
+    return poly ? launch_attn_tc<__nv_bfloat16, true>(tm, ctx, tiles, n_tiles, num_heads, window_half, scale, err, st)
+                : launch_attn_tc<__nv_bfloat16, false>(tm, ctx, tiles, n_tiles, num_heads, window_half, scale, err, st);
+  return poly ? launch_attn_tc<__half, true>(tm, ctx, tiles, n_tiles, num_heads, window_half, scale, err, st)
+              : launch_attn_tc<__half, false>(tm, ctx, tiles, n_tiles, num_heads, window_half, scale, err, st);
+}
+
+cudaError_t exp2_poly_eval(const float* x, float* y, int64_t n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 4096);
+  exp2_poly_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(x, y, n);
+  return cudaGetLastError();
 }
 
 void attention_set_stall(int enable, long long wait_limit_cycles) {

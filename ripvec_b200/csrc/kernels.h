@@ -102,6 +102,9 @@ int fill_attention_tiles(const int* cu_seqlens, int n_seqs, int2* out);
 // the score signal of each CTA's first tile and bounds its waits by wait_limit_cycles, so the
 // launch ends through its bounded-wait exit and reports kErrWaitTimeout.
 void attention_set_stall(int enable, long long wait_limit_cycles);
+// Test hook: y = exp2_poly(x) on n floats (device pointers), the FMA-pipe exponential that the
+// tcgen05 attention's softmax uses beside the MUFU ex2 when RV_ATTN_EXP2_POLY=1.
+cudaError_t exp2_poly_eval(const float* x, float* y, int64_t n, cudaStream_t st);
 
 // f32 -> 16-bit conversion (weights upload), n elements.
 cudaError_t convert_f32(Act act, const float* in, void* out, int64_t n, cudaStream_t st);

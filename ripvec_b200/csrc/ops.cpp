@@ -130,6 +130,14 @@ int rv_debug_stall_attention(int32_t enable, int64_t wait_limit_cycles) {
   return RV_OK;
 }
 
+int rv_debug_exp2_poly(const float* x, float* y, int64_t n, void* stream) {
+  if (n < 0 || (n > 0 && (!x || !y))) return RV_E_INVALID;
+  if (n == 0) return RV_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rv::exp2_poly_eval(x, y, n, st) != cudaSuccess) return RV_E_CUDA;
+  return cudaStreamSynchronize(st) == cudaSuccess ? RV_OK : RV_E_CUDA;
+}
+
 int rv_op_layernorm(int32_t act_dtype, const void* in, void* out, int32_t rows, int32_t hidden,
                     const float* gamma, const float* beta, float eps, void* stream) {
   if (act_dtype != RV_DTYPE_BF16 && act_dtype != RV_DTYPE_F16) return RV_E_INVALID;

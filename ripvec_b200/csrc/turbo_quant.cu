@@ -158,16 +158,22 @@ constexpr int scan_threads() {
   return QB == 8 ? 1024 : QB == 4 ? 512 : 256;
 }
 
-// QB consecutive table entries (queries q0..q0+QB-1 of one pair and bin) in one shared load.
+// The QB table entries (queries 0..QB-1 of one pair and bin) in one or two shared loads.  slot()
+// is where query qq of bin `bin` sits among the QB words of its entry: the 8-query tables swap
+// their two 16-byte halves for the bins whose bit 2 is set, so that for each half the 16 bins of a
+// pair fall on all eight 16-byte bank groups instead of four (a warp's lanes read random bins of
+// the same pair, and two lanes on one bank group with different addresses serialise).
 template <int QB>
 struct QVec;
 template <>
 struct QVec<1> {
-  __device__ __forceinline__ static void get(const float* p, float (&v)[1]) { v[0] = *p; }
+  __device__ __forceinline__ static int slot(int qq, int) { return qq; }
+  __device__ __forceinline__ static void get(const float* p, int, float (&v)[1]) { v[0] = *p; }
 };
 template <>
 struct QVec<2> {
-  __device__ __forceinline__ static void get(const float* p, float (&v)[2]) {
+  __device__ __forceinline__ static int slot(int qq, int) { return qq; }
+  __device__ __forceinline__ static void get(const float* p, int, float (&v)[2]) {
     const float2 t = *reinterpret_cast<const float2*>(p);
     v[0] = t.x;
     v[1] = t.y;
@@ -175,7 +181,8 @@ struct QVec<2> {
 };
 template <>
 struct QVec<4> {
-  __device__ __forceinline__ static void get(const float* p, float (&v)[4]) {
+  __device__ __forceinline__ static int slot(int qq, int) { return qq; }
+  __device__ __forceinline__ static void get(const float* p, int, float (&v)[4]) {
     const float4 t = *reinterpret_cast<const float4*>(p);
     v[0] = t.x;
     v[1] = t.y;
@@ -185,9 +192,11 @@ struct QVec<4> {
 };
 template <>
 struct QVec<8> {
-  __device__ __forceinline__ static void get(const float* p, float (&v)[8]) {
-    const float4 a = *reinterpret_cast<const float4*>(p);
-    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  __device__ __forceinline__ static int slot(int qq, int bin) { return qq ^ (bin & 4); }
+  __device__ __forceinline__ static void get(const float* p, int bin, float (&v)[8]) {
+    const int sw = bin & 4;  // 0, or 4 when the halves are swapped
+    const float4 a = *reinterpret_cast<const float4*>(p + sw);
+    const float4 b = *reinterpret_cast<const float4*>(p + (4 - sw));
     v[0] = a.x;
     v[1] = a.y;
     v[2] = a.z;
@@ -201,8 +210,8 @@ struct QVec<8> {
 
 // Warp w of the grid scores row groups g = w, w + warps, ... of [g_begin, g_begin + g_count):
 // lane l owns row 32 g + l.  The QB queries of a pass share each loaded code word; their tables
-// sit interleaved in shared memory, lut_s[(pair * levels + bin) * QB + query], so one load
-// brings the entries of all QB queries.  Scores go to s[qq * ld + 32 (g - g_begin) + l] for the
+// sit interleaved in shared memory, lut_s[(pair * levels + bin) * QB + QVec<QB>::slot(query, bin)],
+// so one load (two for 8 queries) brings the entries of all QB queries.  Scores go to s[qq * ld + 32 (g - g_begin) + l] for the
 // rows inside the first `valid` of the launch.
 template <int QB>
 __global__ void __launch_bounds__(scan_threads<QB>()) polar_scan_kernel(
@@ -213,7 +222,7 @@ __global__ void __launch_bounds__(scan_threads<QB>()) polar_scan_kernel(
   const int tab = pairs * levels;
 #pragma unroll
   for (int qq = 0; qq < QB; ++qq)
-    for (int r = threadIdx.x; r < tab; r += blockDim.x) lut_s[r * QB + qq] = lut[qq * tab + r];
+    for (int r = threadIdx.x; r < tab; r += blockDim.x) lut_s[r * QB + QVec<QB>::slot(qq, r % levels)] = lut[qq * tab + r];
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int p4n = pairs / 4, p16n = pairs / 16;
@@ -239,7 +248,7 @@ __global__ void __launch_bounds__(scan_threads<QB>()) polar_scan_kernel(
         const float4 r4 = rv4[j >> 2];
         const float rad = (j & 3) == 0 ? r4.x : (j & 3) == 1 ? r4.y : (j & 3) == 2 ? r4.z : r4.w;
         float t[QB];
-        QVec<QB>::get(row_tab + (j * levels + code) * QB, t);
+        QVec<QB>::get(row_tab + (j * levels + code) * QB, code, t);
 #pragma unroll
         for (int qq = 0; qq < QB; ++qq) acc[qq] = __fadd_rn(acc[qq], __fmul_rn(rad, t[qq]));
       }

@@ -69,6 +69,10 @@ def test_search_entry_points_reject_a_null_index_without_a_device(lib):
     assert lib.rv_index_topk_noalloc(None, None, 1, 10, 0.0, None, None, None, None) == inv
     assert lib.rv_index_topk_noalloc(None, None, 0, 10, 0.0, None, None, None, None) == inv
     assert lib.rv_index_last_error(None) == b"null index"
+    # the exponential test hook checks its arguments before it touches a device
+    assert lib.rv_debug_exp2_poly(None, None, 0, None) == _lib.RV_OK
+    assert lib.rv_debug_exp2_poly(None, None, 4, None) == inv
+    assert lib.rv_debug_exp2_poly(None, None, -1, None) == inv
 
 
 def test_noalloc_argument_checks_without_a_device(lib):

@@ -70,18 +70,20 @@ def _attention_ref(qkv: np.ndarray, cu, heads, hd, window_half):
     return out
 
 
-@pytest.mark.parametrize("impl", ["tc", "mma"])
+@pytest.mark.parametrize("impl", ["tc", "tc_poly", "mma"])
 @pytest.mark.parametrize("act", ["bf16", "f16"])
 @pytest.mark.parametrize("hd,heads,window", [(64, 12, -1), (64, 12, 64), (32, 12, -1), (64, 4, 64)])
 def test_attention_matches_oracle(cuda_device, monkeypatch, impl, act, hd, heads, window):
-    """head_dim 64 runs the tcgen05 kernel ("tc") or, with RV_ATTN_TC=0, the mma.sync kernel;
-    head_dim 32 has only the mma.sync kernel."""
+    """head_dim 64 runs the tcgen05 kernel ("tc"; "tc_poly" with a quarter of the softmax
+    exponentials on the FMA pipe, RV_ATTN_EXP2_POLY=1) or, with RV_ATTN_TC=0, the mma.sync
+    kernel; at this op level head_dim 32 has only the mma.sync kernel."""
     torch = _torch()
     from ripvec_b200 import _lib as L
 
-    if impl == "tc" and hd != 64:
+    if impl != "mma" and hd != 64:
         pytest.skip("the tcgen05 kernel covers head_dim 64")
-    monkeypatch.setenv("RV_ATTN_TC", "1" if impl == "tc" else "0")
+    monkeypatch.setenv("RV_ATTN_TC", "0" if impl == "mma" else "1")
+    monkeypatch.setenv("RV_ATTN_EXP2_POLY", "1" if impl == "tc_poly" else "0")
 
     lengths = [1, 17, 63, 64, 65, 129, 300, 512, 0, 700]
     cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
@@ -141,3 +143,32 @@ def test_layernorm_matches_fp32(cuda_device, hidden):
                                    beta.data_ptr(), 1e-5, _stream()) == 0
     ref = torch.nn.functional.layer_norm(x.float(), (hidden,), gamma, beta, 1e-5)
     assert (y.float() - ref).abs().max().item() < 3e-2
+
+
+def test_exp2_poly_error_bound(cuda_device):
+    """The FMA-pipe exponential of the tcgen05 softmax (rv_debug_exp2_poly) against the exact
+    2^x (float64) and CUDA's exp2f (torch.exp2 on the device) over the softmax input range: relative
+    error below 7.6e-5 on [-125, 126] (the polynomial's minimax error is 7.48e-5), and exactly 0
+    below -125 and for masked (-inf) scores."""
+    torch = _torch()
+    from ripvec_b200 import _lib as L
+
+    rng = np.random.default_rng(5)
+    x = np.concatenate([np.linspace(-125.0, 126.0, 2_000_001), rng.uniform(-20.0, 8.0, 1_000_000),
+                        np.arange(-125, 127, dtype=np.float64), np.arange(-125, 127) + 0.5,
+                        [0.0, -0.0, 1e-30, -1e-30, 8.0]]).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty_like(xd)
+    assert L.lib().rv_debug_exp2_poly(xd.data_ptr(), yd.data_ptr(), x.size, _stream()) == L.RV_OK
+    y = yd.cpu().numpy().astype(np.float64)
+    exact = np.exp2(x.astype(np.float64))
+    rel = np.abs(y - exact) / exact
+    assert rel.max() < 7.6e-5, (rel.max(), x[np.argmax(rel)])
+    cuda = torch.exp2(xd).cpu().numpy().astype(np.float64)
+    assert (np.abs(y - cuda) / cuda).max() < 7.6e-5 + 2.0 ** -21
+
+    low = np.array([-125.0001, -126.0, -200.0, -1e9, -np.inf], np.float32)
+    ld = torch.from_numpy(low).cuda()
+    lo = torch.full_like(ld, 1.0)
+    assert L.lib().rv_debug_exp2_poly(ld.data_ptr(), lo.data_ptr(), low.size, _stream()) == L.RV_OK
+    assert (lo.cpu().numpy() == 0.0).all()
