@@ -402,6 +402,7 @@ void rv_index_destroy(rv_index* x) {
     x->rank_i.release();
     x->rank_i2.release();
     x->rank_tmp.release();
+    if (x->order_ev) cudaEventDestroy(x->order_ev);
     if (x->stream) cudaStreamDestroy(x->stream);
   }
   delete x;
@@ -818,12 +819,15 @@ int rv_index_rank_cascade(rv_index* x, const float* queries, int32_t nq, int32_t
     if (!x->c_q.reserve(size_t(nq) * t) || !x->c_oi.reserve(size_t(nq) * pre) || !x->c_os.reserve(size_t(nq) * pre) ||
         !x->qb.reserve(size_t(nq) * x->dim) || !x->cnt.reserve(size_t(nq)) || !x->guard.reserve(size_t(nq)))
       return ifail(x, RV_E_NOMEM, "cascade buffers");
-    // Phase 1: exact top-pre of the truncated queries over the truncated rows.
+    // Phase 1: exact top-pre of the truncated queries over the truncated rows, on the truncated
+    // index's stream, ordered after the query transform by an event (no host synchronisation).
     IX_TRY(x, rv::cascade_queries(x->qf.p, nq, x->dim, t, x->c_q.p, st));
-    IX_TRY(x, cudaStreamSynchronize(st));
+    if (!x->order_ev) IX_TRY(x, cudaEventCreateWithFlags(&x->order_ev, cudaEventDisableTiming));
+    IX_TRY(x, cudaEventRecord(x->order_ev, st));
     {
       std::lock_guard<std::mutex> lc(c->mu);
       c->base = x->base;
+      IX_TRY(x, cudaStreamWaitEvent(c->stream, x->order_ev, 0));
       rc = topk_device(c, x->c_q.p, nq, pre, -INFINITY, x->c_oi.p, x->c_os.p, nullptr, nullptr);
       if (rc) return ifail(x, rc, "cascade first phase: " + c->err);
       // Phase 2: exact rescoring of the candidates with the full rows (index.rs:287-296).
@@ -833,9 +837,9 @@ int rv_index_rank_cascade(rv_index* x, const float* queries, int32_t nq, int32_t
                                  x->n, 0.0, threshold, x->oi.p, x->os.p, out_score64 ? x->os64.p : nullptr,
                                  x->cnt.p, x->guard.p, st));
       x->launches += 3;
+      // The counts come back with the results below (one synchronisation for both).
       counts.resize(nq);
       IX_TRY(x, cudaMemcpyAsync(counts.data(), x->cnt.p, sizeof(int) * nq, cudaMemcpyDeviceToHost, st));
-      IX_TRY(x, cudaStreamSynchronize(st));
     }
     rc = RV_OK;
   }

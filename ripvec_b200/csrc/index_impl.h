@@ -78,5 +78,8 @@ struct rv_index {
   DevBuf<uint8_t> rank_tmp;
   int64_t launches = 0;
   bool filter_off = false;  // RV_SCAN_FILTER=0 at creation
+  // Orders work queued on another index's stream (the cascade's truncated index) after this
+  // index's stream without a host synchronisation; created on first use.
+  cudaEvent_t order_ev = nullptr;
 };
 
