@@ -472,8 +472,9 @@ int alloc_workspaces(rv_ctx* c) {
       !rv::make_tmap_2d_16bit(&c->map_c, c->cbuf, bf, c->attn_width, T, uint64_t(c->attn_width) * 2, 64, 128,
                               &why) ||
       !rv::make_tmap_2d_16bit(&c->map_act, c->act, bf, I, T, uint64_t(I) * 2, 64, 128, &why) ||
-      !rv::make_tmap_2d_16bit(&c->map_qkv_out, c->qkv, bf, 3 * H, T, uint64_t(3 * H) * 2, 64, 128, &why) ||
-      !rv::make_tmap_2d_16bit(&c->map_act_out, c->act, bf, I, T, uint64_t(I) * 2, 32, 128, &why, 64))
+      !rv::make_tmap_2d_16bit(&c->map_qkv_out, c->qkv, bf, 3 * H, T, uint64_t(3 * H) * 2, 64, 32, &why) ||
+      !rv::make_tmap_2d_16bit(&c->map_x_out, c->x, bf, H, T, uint64_t(H) * 2, 64, 32, &why) ||
+      !rv::make_tmap_2d_16bit(&c->map_act_out, c->act, bf, I, T, uint64_t(I) * 2, 32, 32, &why, 64))
     return fail(c, RV_E_CUDA, why);
   return RV_OK;
 }
@@ -504,7 +505,7 @@ int gemm(rv_ctx* c, const CUtensorMap& A, const rv::DeviceMatrix& B, int M, Gemm
   a.eps = c->d.norm_eps;
   if (a.pair && c->tma_epi) {
     if (epi == GemmEpi::kQkvRope || epi == GemmEpi::kNormQkvRope) a.tmC = &c->map_qkv_out;
-    else if (epi == GemmEpi::kResidualStats) a.tmC = &c->map_x;
+    else if (epi == GemmEpi::kResidualStats) a.tmC = &c->map_x_out;
     else if (epi == GemmEpi::kNormGeglu) a.tmC = &c->map_act_out;
   }
   RV_LAUNCH_K(c, RV_KIND_GEMM, 2.0 * double(M) * a.N * a.K, rv::gemm_tc(c->adt, a, c->d_err, c->stream));

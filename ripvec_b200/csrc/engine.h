@@ -115,7 +115,9 @@ struct rv_ctx {
   int* meta_h = nullptr;  // pinned staging of meta_d
   cudaEvent_t meta_evt = nullptr;
   CUtensorMap map_x, map_hn, map_c, map_act;
-  CUtensorMap map_qkv_out, map_act_out;  // TMA-staged epilogue outputs (x uses map_x)
+  // TMA-staged epilogue outputs: 32-row boxes, one per epilogue warp (x_out is the residual
+  // stream, read and written by the residual epilogues).
+  CUtensorMap map_qkv_out, map_act_out, map_x_out;
   bool tma_epi = true;                   // TMA-staged GEMM epilogues (RV_TMA_EPI=0 turns off)
   bool attn_tc = true;                   // tcgen05 attention (RV_ATTN_TC=0 turns off)
   // Columns of each of Q, K, V in qkv and of the attention context cbuf: hidden, or heads x 64

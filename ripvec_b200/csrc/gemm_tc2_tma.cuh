@@ -4,12 +4,13 @@
 // into two TMEM accumulators.  Epilogue: two warpgroups of 128 threads, warpgroup e draining
 // accumulator e (every other tile), so two tiles' epilogues run at once.  Each processes its
 // 128 x 256 block in four 64-column groups through its own ring of two 16 KB shared-memory
-// tiles.  When the epilogue reads the output as well (residual add), one thread TMA-loads the
-// next group's 128 x 64 block of C into the ring one group ahead; every thread then combines its
-// row with its accumulator columns, writes the result into the same tile (128-byte swizzled,
-// bank-conflict free), and after a named barrier the same thread TMA-stores the tile.  Epilogue
-// threads never wait on global memory; the accumulator is released as soon as the last TMEM load
-// of a tile is done.
+// tiles, and within it each warp handles its own 32 rows: when the epilogue reads the output as
+// well (residual add), the warp's lane 0 TMA-loads the warp's 32 x 64 block of C into its part of
+// the ring one group ahead; every thread then combines its row with its accumulator columns and
+// writes the result into the same place (128-byte swizzled, bank-conflict free), and lane 0
+// TMA-stores the warp's 32 rows (the output tensor maps have 32-row boxes).  No barrier couples
+// the warps; epilogue threads never wait on global memory; the accumulator is released as soon as
+// the last TMEM load of a tile is done.
 #pragma once
 
 #include "gemm_epi_tma.cuh"
@@ -25,6 +26,7 @@ struct Gemm2TmaCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;  // 32 KB
   static constexpr int kStages = 4;
   static constexpr int kEpiGroups = 2;                    // epilogue warpgroups (one per accumulator)
+  static constexpr int kEpiWarps = 4 * kEpiGroups;
   static constexpr int kRing = 2;                         // staging tiles per epilogue warpgroup
   static constexpr int kRingBytes = 16384;                // 128 rows x 128 B
   static constexpr uint32_t kTmemCols = 512;
@@ -49,22 +51,6 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-// Named barrier `id` over the 128 threads of one epilogue warpgroup that also returns the OR of
-// `fail` over them, so that every thread takes the same exit decision (no thread is ever left
-// alone at a barrier).
-__device__ __forceinline__ bool epi_bar_any(int id, bool fail) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, %2, 128, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}\n"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(fail)), "r"(id)
-      : "memory");
-  return r != 0;
-}
-
 // Byte offset of 16-byte chunk j of row r in a tile written by TMA with 128-byte (rows of 128 B)
 // or 64-byte (rows of 64 B) swizzling; the tile base is 1024-byte aligned.
 template <int kRowBytes>
@@ -96,10 +82,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2TmaCfg::kThread
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* rfull = drain + 1;  // [kEpiGroups][kRing]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + Cfg::kEpiGroups * Cfg::kRing);
+  uint64_t* rfull = drain + 1;  // [epilogue warp][kRing]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rfull + Cfg::kEpiWarps * Cfg::kRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* epi_smem = reinterpret_cast<float*>(ring + Cfg::kEpiGroups * Cfg::kRing * Cfg::kRingBytes + 256);
+  static_assert((2 * kStages + 2 + 2 + 1 + Cfg::kEpiWarps * Cfg::kRing) * 8 + 8 <= 256, "barrier area");
 
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -116,7 +103,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2TmaCfg::kThread
       mbar_init(&tempty[a], 8);
     }
     mbar_init(drain, 1);
-    for (int b = 0; b < Cfg::kEpiGroups * Cfg::kRing; ++b) mbar_init(&rfull[b], 1);
+    for (int b = 0; b < Cfg::kEpiWarps * Cfg::kRing; ++b) mbar_init(&rfull[b], 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -201,16 +188,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2TmaCfg::kThread
     }
   } else {
     // ---------------------------------------------------------------- epilogue (2 x 128 threads)
-    // Epilogue warpgroup ewg drains accumulator ewg, i.e. every other tile of the CTA, through
-    // its own staging ring, barriers and TMA-issuing thread; the two warpgroups work on
-    // consecutive tiles at the same time.
+    // Epilogue warpgroup ewg drains accumulator ewg, i.e. every other tile of the CTA; the two
+    // warpgroups work on consecutive tiles at the same time.  Each warp owns its 32 rows (its
+    // TMEM lane quadrant) of every 64-column group: its lane 0 TMA-loads the warp's rows of C one
+    // group ahead (when the epilogue reads the output) into the warp's 32-row part of the
+    // warpgroup's staging tile and TMA-stores the warp's results from there, so the four warps of
+    // a warpgroup never wait for one another.
     const int ewg = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int rl = quad * 32 + lane;             // row inside this CTA's 128-row block = TMEM lane
-    const int bar_id = 1 + ewg;
-    const bool e0 = threadIdx.x == 64 + 128 * ewg;  // issues this warpgroup's TMA loads and stores
-    uint8_t* ring_e = ring + ewg * Cfg::kRing * Cfg::kRingBytes;
-    uint64_t* rfull_e = rfull + ewg * Cfg::kRing;
+    constexpr uint32_t kSubBytes = 32 * kRowBytes;  // this warp's 32 rows of a staging tile
+    uint8_t* ring_w = ring + ewg * Cfg::kRing * Cfg::kRingBytes + quad * kSubBytes;
+    uint64_t* rfull_w = rfull + (warp - 2) * Cfg::kRing;
     const uint32_t tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
     epi.stage(epi_smem, threadIdx.x - 64, 128 * Cfg::kEpiGroups);
     asm volatile("bar.sync 3, %0;" ::"n"(128 * Cfg::kEpiGroups) : "memory");
@@ -220,13 +209,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2TmaCfg::kThread
     const int total_groups = ew_tiles * kGroups;
     // Group q of this warpgroup: its (q / kGroups)-th tile, i.e. CTA tile it = 2 (q / kGroups) + ewg.
     auto group_tile = [&](int q) { return cluster_id + (Cfg::kEpiGroups * (q / kGroups) + ewg) * num_clusters; };
-    if (Epi::kReadsC && e0 && total_groups > 0) {
+    // First output row of this warp in tile t.
+    auto warp_row0 = [&](int t) { return (t / num_n) * (2 * kGemmBM) + static_cast<int>(rank) * kGemmBM + quad * 32; };
+    if (Epi::kReadsC && lane == 0 && total_groups > 0) {
       const int t = group_tile(0);
-      mbar_arrive_expect_tx(&rfull_e[0], Cfg::kRingBytes);
-      tma_load_2d(ring_e, &tmC, &rfull_e[0], (t % num_n) * kBN, (t / num_n) * (2 * kGemmBM) + int(rank) * kGemmBM);
+      mbar_arrive_expect_tx(&rfull_w[0], kSubBytes);
+      tma_load_2d(ring_w, &tmC, &rfull_w[0], (t % num_n) * kBN, warp_row0(t));
     }
     bool ok = true;
-    int last_load = Epi::kReadsC && total_groups > 0 ? 0 : -1;  // newest group whose C load is in flight
+    int last_load = Epi::kReadsC && total_groups > 0 ? 0 : -1;  // newest group whose C load is in flight (lane 0)
     typename Epi::Tile tile;
     for (int q = 0; q < total_groups; ++q) {
       const int g = q % kGroups;
@@ -239,18 +230,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2TmaCfg::kThread
       const int row = m0 + rl;
       const bool live = row < M;
       const int b = q % Cfg::kRing;
-      uint8_t* buf = ring_e + b * Cfg::kRingBytes;
-      if (e0 && Epi::kReadsC && q + 1 < total_groups) {
-        // C of group q + 1 goes into slot (q + 1) % 2, which group q - 1's store reads.
+      uint8_t* buf = ring_w + b * Cfg::kRingBytes;
+      if (lane == 0 && Epi::kReadsC && q + 1 < total_groups) {
+        // C of group q + 1 goes into slot (q + 1) % 2, which this warp's store of group q - 1 reads.
         bulk_wait_read<0>();
-        {
-          const int qn = q + 1, tn = group_tile(qn), bn = qn % Cfg::kRing;
-          fence_proxy_async();
-          mbar_arrive_expect_tx(&rfull_e[bn], Cfg::kRingBytes);
-          tma_load_2d(ring_e + bn * Cfg::kRingBytes, &tmC, &rfull_e[bn], (tn % num_n) * kBN + (qn % kGroups) * 64,
-                      (tn / num_n) * (2 * kGemmBM) + int(rank) * kGemmBM);
-          last_load = qn;
-        }
+        const int qn = q + 1, tn = group_tile(qn), bn = qn % Cfg::kRing;
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&rfull_w[bn], kSubBytes);
+        tma_load_2d(ring_w + bn * Cfg::kRingBytes, &tmC, &rfull_w[bn], (tn % num_n) * kBN + (qn % kGroups) * 64,
+                    warp_row0(tn));
+        last_load = qn;
       }
       bool fail = false;
       if (g == 0) {
@@ -274,12 +263,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2TmaCfg::kThread
       }
       float r[64];
       if (Epi::kReadsC && !fail) {
-        const bool w = mbar_wait(&rfull_e[b], (q / Cfg::kRing) & 1, abort_flag);
+        const bool w = mbar_wait(&rfull_w[b], (q / Cfg::kRing) & 1, abort_flag);
         fail = !__all_sync(0xffffffffu, w);
         if (!fail) {
 #pragma unroll
           for (int jj = 0; jj < 8; ++jj)
-            unpack8<T>(*reinterpret_cast<const uint4*>(buf + swz<128>(rl, jj)), &r[8 * jj]);
+            unpack8<T>(*reinterpret_cast<const uint4*>(buf + swz<128>(lane, jj)), &r[8 * jj]);
         }
       }
       if (!fail) {
@@ -287,32 +276,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2TmaCfg::kThread
 #pragma unroll
         for (int jj = 0; jj < kOutCols / 8; ++jj) {
           const float* v = (jj < 4) ? &v0[8 * jj] : &v1[8 * (jj - 4)];
-          *reinterpret_cast<uint4*>(buf + swz<kRowBytes>(rl, jj)) = pack8<T>(v);
+          *reinterpret_cast<uint4*>(buf + swz<kRowBytes>(lane, jj)) = pack8<T>(v);
         }
       }
       fence_proxy_async();
-      // Group q + 1 overwrites slot (q + 1) % 2 = (q - 1) % 2 as soon as this barrier opens, so the
-      // store of group q - 1 must have read it before (stores up to q - 1 are the outstanding ones).
-      if (e0) bulk_wait_read<0>();
-      if (epi_bar_any(bar_id, fail || *abort_flag != 0)) {
+      if (__any_sync(0xffffffffu, fail || *abort_flag != 0)) {  // a warp-uniform exit decision
         ok = false;
         break;
       }
-      if (e0) {
+      __syncwarp();  // the warp's rows are in the staging tile before lane 0 stores them
+      if (lane == 0) {
         const int out_col = (kOutCols == 64) ? n0 + g * 64 : (n0 + g * 64) / 2;
-        tma_store_2d(&tmC, buf, out_col, m0);
+        tma_store_2d(&tmC, buf, out_col, m0 + quad * 32);
         bulk_commit();
+        // Group q + 1 overwrites slot (q + 1) % 2 = (q - 1) % 2: this warp's store of group q - 1
+        // has read it once at most the newest store (group q) is outstanding.
+        bulk_wait_read<1>();
       }
+      __syncwarp();
     }
-    if (!ok && e0 && last_load >= 0) {  // let the C load still in flight land (bounded)
+    if (!ok && lane == 0 && last_load >= 0) {  // let the C load still in flight land (bounded)
       volatile int no_abort = 0;
-      mbar_wait(&rfull_e[last_load % Cfg::kRing], (last_load / Cfg::kRing) & 1, &no_abort);
+      mbar_wait(&rfull_w[last_load % Cfg::kRing], (last_load / Cfg::kRing) & 1, &no_abort);
     }
     if (!ok && lane == 0) {
       *abort_flag = 1;
       atomicOr(err, kErrWaitTimeout);
     }
-    if (e0) bulk_wait_all();  // every store has landed before the kernel ends
+    if (lane == 0) bulk_wait_all();  // every store of this warp has landed before the kernel ends
   }
 
   __syncthreads();

@@ -34,8 +34,8 @@ enum class GemmEpi {
 struct GemmArgs {
   const CUtensorMap* tmA;  // A [M,K] K-major, box 64 x 128
   const CUtensorMap* tmB;  // B [N,K] K-major, box 64 x BN
-  const CUtensorMap* tmC;  // optional: output C for the TMA-staged epilogue (box 64 x 128, 128-B
-                           // swizzle; 32 x 128 with 64-B swizzle for GeGLU)
+  const CUtensorMap* tmC;  // optional: output C for the TMA-staged epilogue (box 64 x 32, 128-B
+                           // swizzle; 32 x 32 with 64-B swizzle for GeGLU: one box per warp)
   int M, N, K;
   int bn;                  // 128 or 256 (N % bn == 0)
   int b_row_offset;        // added to the B-operand row coordinate (chunked scans)
