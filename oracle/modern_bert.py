@@ -19,6 +19,9 @@ the first ``total_tokens`` ids of the padded array (``modern_bert.rs:901-902``,
 
 from __future__ import annotations
 
+import contextlib
+import os
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass
 
 import numpy as np
@@ -62,6 +65,19 @@ def weight_names(cfg: ModernBertConfig) -> list[str]:
 _Q_BLOCK = 512  # query rows per score block: keeps [block, L] f32 small at L = 8192
 
 
+@contextlib.contextmanager
+def _single_threaded_blas():
+    """One BLAS thread per call while the attention heads run on their own threads (the small
+    per-block GEMMs gain nothing from more, and nested pools would oversubscribe the cores)."""
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:
+        yield
+        return
+    with threadpool_limits(limits=1, user_api="blas"):
+        yield
+
+
 def _attention(q, k, v, scale, window_half, dt):
     """``q,k,v [L, heads, d]`` -> context ``[L, heads*d]``.  ``window_half < 0`` means global.
 
@@ -77,7 +93,8 @@ def _attention(q, k, v, scale, window_half, dt):
     L, nh, d = q.shape
     ctx = np.empty((L, nh, d), dtype=q.dtype)
     sc = dt(scale)
-    for h in range(nh):
+
+    def head(h):
         qh = np.ascontiguousarray(q[:, h, :])
         kh = np.ascontiguousarray(k[:, h, :])
         vh = np.ascontiguousarray(v[:, h, :])
@@ -89,6 +106,17 @@ def _attention(q, k, v, scale, window_half, dt):
                 far = np.abs(np.arange(i0, i1)[:, None] - np.arange(j0, j1)[None, :]) > window_half
                 s = s + np.where(far, dt(-1e9), dt(0.0))
             ctx[i0:i1, h, :] = ops.softmax_rows(s) @ vh[j0:j1]
+
+    # The heads are independent and write disjoint slices of ctx, so they run on a thread pool
+    # (numpy releases the GIL inside these array operations); each head's arithmetic is the same
+    # as in a sequential loop.  Long chunks only: short ones are not worth the threads.
+    workers = min(nh, os.cpu_count() or 1) if L >= 1024 else 1
+    if workers <= 1:
+        for h in range(nh):
+            head(h)
+    else:
+        with _single_threaded_blas(), ThreadPoolExecutor(max_workers=workers) as pool:
+            list(pool.map(head, range(nh)))
     return ctx.reshape(L, nh * d)
 
 
