@@ -108,8 +108,9 @@ def _attention(q, k, v, scale, window_half, dt):
             ctx[i0:i1, h, :] = ops.softmax_rows(s) @ vh[j0:j1]
 
     # The heads are independent and write disjoint slices of ctx, so they run on a thread pool
-    # (numpy releases the GIL inside these array operations); each head's arithmetic is the same
-    # as in a sequential loop.  Long chunks only: short ones are not worth the threads.
+    # (numpy releases the GIL inside these array operations); each head's arithmetic is that of a
+    # sequential loop with one BLAS thread per call (the BLAS thread count can change the last
+    # bits of a GEMM, as for any BLAS caller).  Long chunks only: short ones are not worth it.
     workers = min(nh, os.cpu_count() or 1) if L >= 1024 else 1
     if workers <= 1:
         for h in range(nh):

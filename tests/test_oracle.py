@@ -179,3 +179,22 @@ def test_bf16_rounding_is_nearest_even():
     x = np.array([1.0, 1.00390625, 1.01171875, -2.5, 3.0e38, np.inf], np.float32)
     r = ops.to_bf16(x)
     assert r[0] == 1.0 and r[1] == 1.0 and r[2] == 1.015625 and r[3] == -2.5 and np.isinf(r[5])
+
+
+@pytest.mark.parametrize("window_half", [-1, 64])
+def test_threaded_oracle_attention_is_bit_identical_to_the_sequential_loop(monkeypatch, window_half):
+    """The oracle runs the attention heads of long chunks on a thread pool, with one BLAS thread
+    per call; every head must come out exactly as the sequential loop computes it with the same
+    BLAS setting.  (The BLAS thread count itself can change the last bits of a GEMM, as for any
+    BLAS caller: with several BLAS threads the sequential loop differs by about 1e-7 here.)"""
+    from oracle import modern_bert
+
+    rng = np.random.default_rng(11)
+    L, nh, d = 1100, 4, 64
+    q, k, v = (rng.standard_normal((L, nh, d)).astype(np.float32) for _ in range(3))
+    threaded = modern_bert._attention(q, k, v, 0.125, window_half, np.float32)
+    monkeypatch.setattr(modern_bert.os, "cpu_count", lambda: 1)
+    with modern_bert._single_threaded_blas():
+        sequential = modern_bert._attention(q, k, v, 0.125, window_half, np.float32)
+    np.testing.assert_array_equal(threaded, sequential)
+    np.testing.assert_allclose(threaded, modern_bert._attention(q, k, v, 0.125, window_half, np.float32), atol=1e-6)
